@@ -1,0 +1,92 @@
+"""Tiny known-answer ROMs and snapshots, restating the fixtures the reference's
+own C++ tests build in code (tests/cpp/test_cpu.cpp, test_console.cpp,
+test_cuda_batch.cpp, test_cuda_batch_console.cpp).  Shared by the checker
+pin tests (CPU) and the GPU parity tests, so both sides run the same inputs.
+"""
+from __future__ import annotations
+
+import struct
+
+from nesle_b200 import workloads as w
+
+
+def rom_with(code: dict[int, bytes], reset: int = 0x8000, nmi: int = 0x9000,
+             irq: int = 0x9000, chr_rom: bytes | None = None, flags6: int = 0x01) -> bytes:
+    """32 KB NROM image filled with NOP ($EA), code placed at CPU addresses."""
+    prg = bytearray([0xEA]) * 32768
+    for addr, data in code.items():
+        prg[addr - 0x8000: addr - 0x8000 + len(data)] = data
+    prg[0x7FFA:0x7FFC] = struct.pack("<H", nmi)
+    prg[0x7FFC:0x7FFE] = struct.pack("<H", reset)
+    prg[0x7FFE:0x8000] = struct.pack("<H", irq)
+    return w.ines_image(bytes(prg), chr_rom if chr_rom is not None else bytes(8192), flags6)
+
+
+def asm(base: int, *lines) -> bytes:
+    a = w.Asm(base)
+    for ln in lines:
+        if isinstance(ln, bytes):
+            a.raw(ln)
+        else:
+            a.emit(*ln)
+    return a.assemble()[0]
+
+
+# test_cpu.cpp:34-56  LDA #$41 / TAX / INX / STA $0200 -> cycles 2,2,2,4
+LDA_TAX_INX_STA = rom_with({0x8000: asm(0x8000, ("LDA", w.IMM, 0x41), ("TAX",), ("INX",),
+                                        ("STA", w.ABS, 0x0200), ("JMP", w.ABS, 0x800A))})
+
+# test_cpu.cpp:58-76  JSR $9000 / (LDA #$77 / RTS) / STA $10
+JSR_RTS = rom_with({0x8000: asm(0x8000, ("JSR", w.ABS, 0x9000), ("STA", w.ZP, 0x10),
+                                ("JMP", w.ABS, 0x8005)),
+                    0x9000: asm(0x9000, ("LDA", w.IMM, 0x77), ("RTS",))}, nmi=0xA000)
+
+# test_cpu.cpp:78-86  BNE +1 at $80FD, taken across a page: 4 cycles, pc=$8100
+BNE_PAGE_CROSS = rom_with({0x80FD: bytes([0xD0, 0x01]), 0x8100: asm(0x8100, ("JMP", w.ABS, 0x8100))},
+                          reset=0x80FD)
+
+# test_cpu.cpp:88-101  SEC / LDA #$10 / SBC #$01 -> A=$0F, C=1
+SEC_SBC = rom_with({0x8000: asm(0x8000, ("SEC",), ("LDA", w.IMM, 0x10), ("SBC", w.IMM, 0x01),
+                                ("JMP", w.ABS, 0x8005))})
+
+# test_console.cpp:72-92 / test_cuda_batch_console.cpp  NMI: INC $00 / RTI at $9000
+NMI_ROM = rom_with({0x8000: asm(0x8000, ("LDA", w.IMM, 0x80), ("STA", w.ABS, 0x2000),
+                                ("JMP", w.ABS, 0x8005)),
+                    0x9000: asm(0x9000, ("INC", w.ZP, 0x00), ("RTI",))})
+
+# test_console.cpp:94-110  LDA #$02 / STA $4014 -> 2 then 517 CPU cycles
+DMA_ROM = rom_with({0x8000: asm(0x8000, ("LDA", w.IMM, 0x02), ("STA", w.ABS, 0x4014),
+                                ("JMP", w.ABS, 0x8005))})
+
+IDLE_ROM = rom_with({0x8000: asm(0x8000, ("JMP", w.ABS, 0x8000))})
+
+
+def dma_snapshot() -> bytes:
+    """PC at $8000 with RAM $0200+i = $FF-i (test_console.cpp:99-101)."""
+    ram = bytearray(2048)
+    for i in range(256):
+        ram[0x200 + i] = 0xFF - i
+    return w.write_fcs(w.Snapshot(pc=0x8000, cpu_ram=bytes(ram)))
+
+
+def mario_snapshot(x_page: int, x_screen: int, timer: int, player_state: int = 8,
+                   y_viewport: int = 1) -> bytes:
+    """RAM laid out like test_cuda_batch.cpp:21-33, PC parked on an idle JMP."""
+    ram = bytearray(2048)
+    ram[0x6D] = x_page
+    ram[0x86] = x_screen
+    ram[0xB5] = y_viewport
+    ram[0x0E] = player_state
+    ram[0x75A] = 2
+    ram[0x7F8:0x7FB] = bytes([timer // 100, (timer // 10) % 10, timer % 10])
+    return w.write_fcs(w.Snapshot(pc=0x8000, cpu_ram=bytes(ram)))
+
+
+# Reward cases of test_cuda_batch.cpp:45-87: (previous x, previous timer) come
+# from the snapshot, the current values are poked into RAM before the step.
+REWARD_CASES = [
+    # prev (page, screen, timer), current (page, screen, timer, player_state), reward, done
+    ((0, 40, 400), (0, 43, 399, 8), 2.0, 0),
+    ((0, 80, 399), (0, 90, 398, 8), -1.0, 0),
+    ((0, 48, 400), (0, 50, 399, 0x0B), -24.0, 1),
+]
