@@ -1,0 +1,366 @@
+#!/usr/bin/env python
+"""Env-step throughput of the B200 batched NES core (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE.json metric "env-steps/s (frameskip 4, 65,536 envs/GPU)"):
+configuration 4 -- 65,536 envs per GPU, RAM observation mode, frameskip 4,
+joypad-driven divergent synthetic ROM, 8 seeded snapshots (global env i starts
+from snapshot i mod 8), uniform u8 actions, done at a per-episode frame limit
+U[500, 5000] with fused auto-reset.  Envs shard across GPUs with no data-path
+collective (weak scaling); under torchrun each rank runs its own 65,536 envs.
+
+value  : device-resident loop -- actions for every step already in HBM, one
+         step_device (C-ABI nesle_step, fused auto-reset) per step, timed with
+         CUDA events on the launching stream, max over ranks.
+e2e    : the public host API CudaBatch.step(actions) per step -- pinned host
+         actions copied in, kernel, rewards and dones read back -- wall clock,
+         max over ranks.
+--impl reference : the reference's own CPU core (nesle::Console compiled
+         unchanged from the reference sources into oracle/_ref/) on all host
+         threads, on a bounded sample of the same workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "env-steps/s (frameskip 4, 65,536 envs/GPU) at 1/2/4/8 B200"
+UNIT = "env-steps/s"
+# Algorithmic HBM bytes of one env-step in RAM mode: one compulsory round trip
+# of the mutable per-env state (2 KB RAM read + write, OAM 256 written, CPU and
+# PPU scalars 88, controller/DMA/reward baselines 30, action 1, reward 4 +
+# done 1) -- see DESIGN.md "Roofline".
+BYTES_PER_ENV_STEP = 4476
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--envs", type=int, default=65536, help="envs per GPU")
+    ap.add_argument("--workload", default="config4", choices=["config4", "config2", "config1"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args(argv)
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+def make_workload(name: str):
+    from nesle_b200 import workloads as w
+
+    return {"config4": w.config4, "config2": w.config2, "config1": w.config1}[name]()
+
+
+def workload_config(wl, envs: int, world: int) -> dict:
+    return {
+        "workload": f"{wl.name}: BASELINE config {wl.name[6]}" if wl.name.startswith("config") else wl.name,
+        "envs_per_gpu": envs,
+        "total_envs": envs * world,
+        "frameskip": wl.frameskip,
+        "observation": "ram (2048 B/env, zero-copy view)",
+        "snapshots": len(wl.snapshots),
+        "done": {0: "smb", 1: "RAM[$FF]==$FF", 2: "frame limit U[500,5000]"}[wl.done_mode],
+        "auto_reset": "fused",
+        "actions": "uniform u8 joypad bytes (counter RNG)" if wl.name.startswith("config4") else "counter RNG",
+        "l2": "state larger than L2 (RAM 128 MiB + records/OAM/PRG-RAM per 65,536 envs); no flush",
+        "parallelism": f"env-sharded dp{world}",
+    }
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region.
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baselines (reference CPU core).
+# ---------------------------------------------------------------------------
+def host_threads() -> int:
+    return max(1, len(os.sched_getaffinity(0)))
+
+
+def reference_cpu_rate(wl, envs_total: int, steps: int, warmup: int, budget_s: float = 15.0) -> dict:
+    """Reference CPU core on a bounded sample of the workload: env-steps/s."""
+    from oracle import Reference, reference_available, Oracle
+
+    threads = host_threads()
+    kind = "reference" if reference_available() else "port"
+    sample_envs = max(threads, 8)
+
+    def make(n, offset):
+        env = np.arange(offset, offset + n)
+        kw = dict(env_to_level=wl.env_to_level(env) if wl.env_to_level else None, done_mode=wl.done_mode,
+                  done_args=wl.done_args, seed=wl.seed, env_offset=offset)
+        if kind == "reference":
+            return Reference("A", n, wl.frameskip, wl.rom.image, wl.snapshots, threads=threads, **kw), env
+        return Oracle(n, wl.frameskip, wl.rom.image, wl.snapshots, **kw), env
+
+    # calibrate: one step of `threads` envs
+    sim, env = make(sample_envs, 0)
+    t0 = time.perf_counter()
+    sim.step(wl.actions(env, 0))
+    dt = time.perf_counter() - t0
+    per_step_budget = budget_s / max(1, steps + warmup)
+    scale = max(1, int(per_step_budget / max(dt, 1e-6)))
+    sample_envs = min(envs_total, sample_envs * scale)
+    sample_envs = max(threads, (sample_envs // threads) * threads)
+    sim, env = make(sample_envs, 0)
+    for s in range(warmup):
+        sim.step(wl.actions(env, s))
+    times = []
+    for s in range(warmup, warmup + steps):
+        t0 = time.perf_counter()
+        sim.step(wl.actions(env, s))
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    rate = sample_envs * steps / total
+    cores = threads if kind == "reference" else 1
+    return {"value": rate, "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{sample_envs} envs x {steps} env-steps (after {warmup} warm-up) of {wl.name}, "
+                      f"{threads} host threads, nesle::Console stepped as NativeConsole.step",
+            "seconds": total}
+
+
+# ---------------------------------------------------------------------------
+# Our arm.
+# ---------------------------------------------------------------------------
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "_fallback": True}
+
+
+def profile_traffic() -> float | None:
+    """DRAM bytes per launch of the step kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "step_kernel_config4.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch_full_size:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def run_ours(args, rank, world, local) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    from nesle_b200 import build as nb
+    from nesle_b200._cuda_core import CudaBatch
+
+    nb.build()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    wl = make_workload(args.workload)
+    n = args.envs
+    offset = rank * n
+    env = np.arange(offset, offset + n)
+    e2l = wl.env_to_level(env) if wl.env_to_level else None
+    batch = CudaBatch(n, wl.frameskip, wl.rom.image, wl.snapshots if wl.snapshots else None,
+                      e2l if len(wl.snapshots) > 1 else None, device=local, done_mode=wl.done_mode,
+                      done_args=wl.done_args, seed=wl.seed, env_offset=offset)
+    total_steps = args.warmup + args.steps
+    acts = torch.from_numpy(np.stack([wl.actions(env, s) for s in range(total_steps)])).to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for s in range(args.warmup):
+        batch.step_device(acts[s], auto_reset=True, synchronize=False)
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    instr = 0
+    with ClockSampler(local) as clocks:
+        time.sleep(0.3)  # let the sampler attach
+        for i, s in enumerate(range(args.warmup, total_steps)):
+            starts[i].record(stream)
+            batch.step_device(acts[s], auto_reset=True, synchronize=False)
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    per_step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    elapsed_ms = starts[0].elapsed_time(ends[-1])
+    instr = int(batch.get_field("stat_instructions").astype(np.int64).sum())  # last step only
+    batch.synchronize()  # raises on illegal-opcode faults
+
+    # e2e through the public host API with pinned host buffers
+    e2e_s = None
+    if not args.no_e2e:
+        host_acts = torch.empty((total_steps, n), dtype=torch.uint8, pin_memory=True)
+        host_acts.copy_(acts.cpu())
+        host_np = host_acts.numpy()
+        for s in range(args.warmup):
+            batch.step(host_np[s], render_frame=False, copy_obs=False)
+        barrier()
+        t0 = time.perf_counter()
+        for s in range(args.warmup, total_steps):
+            out = batch.step(host_np[s], render_frame=False, copy_obs=False)
+        e2e_s = time.perf_counter() - t0
+        assert out["rewards"].shape == (n,)
+        barrier()
+
+    vals = torch.tensor([elapsed_ms, e2e_s or 0.0, float(instr)], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = vals.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = vals.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        elapsed_ms, e2e_s = float(mx[0]), float(mx[1])
+        instr = int(sm[2])
+    clock_summary = clocks.summary()
+
+    result = None
+    if rank == 0:
+        total_env_steps = n * world * args.steps
+        value = total_env_steps / (elapsed_ms / 1e3)
+        kernel_ms = statistics.mean(per_step_ms)
+        peaks = measured_peaks()
+        peak = float(peaks.get("hbm_gbs", 6650.0))
+        achieved = BYTES_PER_ENV_STEP * n / (kernel_ms / 1e3) / 1e9
+        traffic = profile_traffic()
+        sm_mhz = clock_summary.get("sm_mhz") or float(peaks.get("sm_max_mhz", 1965.0))
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": workload_config(wl, n, world),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "note": "of measured HBM copy bandwidth; the kernel is issue-bound (see issue)"},
+            "issue": {"emulated_instructions_per_s": instr / (kernel_ms / 1e3) if instr else None,
+                      "emulated_instructions_per_env_step": instr / (n * world) if instr else None,
+                      "peak_warp_issue_per_s": 148 * 4 * sm_mhz * 1e6},
+            "kernel_ms": kernel_ms,
+            "gpu_launches": args.steps,
+            "clocks": clock_summary,
+        }
+        if e2e_s:
+            result["e2e"] = {"value": total_env_steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": n * world,
+                             "d2h_bytes_per_step": 5 * n * world,
+                             "path": "CudaBatch.step(pinned u8 actions) -> rewards, dones as numpy"}
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = reference_cpu_rate(wl, n, steps=2, warmup=1)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return result
+
+
+def run_reference(args, rank, world, local) -> dict | None:
+    """The reference's CPU implementation of the path on this box's host cores."""
+    if rank != 0:
+        return None
+    wl = make_workload(args.workload)
+    base = reference_cpu_rate(wl, args.envs * world, steps=args.steps, warmup=args.warmup,
+                              budget_s=min(120.0, 6.0 * (args.steps + args.warmup)))
+    return {
+        "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic", "impl": "reference",
+        "config": workload_config(wl, args.envs, world),
+        "cpu_baseline": base,
+        "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        res = run_reference(args, rank, world, local)
+    else:
+        res = run_ours(args, rank, world, local)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

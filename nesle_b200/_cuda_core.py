@@ -1,0 +1,349 @@
+"""Drop-in for the reference's ``nesle._cuda_core`` module, over the C ABI.
+
+Same class and method names, argument meanings and error classes as the
+pybind11 module of hbofz/NeSLE (cpp/bindings/cuda_module.cu:1565-1678):
+``CudaBatch``, ``CudaDeviceArrayView`` and ``parse_fcs_state``.  ValueError
+stands for the binding's std::invalid_argument, RuntimeError for
+std::runtime_error and CUDA errors.
+
+Differences, all additive:
+
+* ``CudaBatch`` takes keyword-only extensions: ``device``, ``done_mode`` and
+  ``done_args`` (the benchmark-configuration done predicates), ``seed``,
+  ``env_offset`` (global index of env 0 when envs are sharded over GPUs) and
+  ``max_instructions_per_frame``.
+* Views report their real device (the reference hard-codes device 0,
+  cuda_module.cu:139,156) and ``__dlpack__(stream)`` makes the consumer stream
+  wait on the producing work instead of synchronising the host.
+* Extra outputs: ``frames_index_device()`` (NES colour indices) and
+  ``obs_gray84_device()`` (84x84 area-resampled luma).
+* Kernels are issued on the caller's current torch stream when torch is
+  imported, else on the legacy default stream like the reference.
+"""
+from __future__ import annotations
+
+import ctypes
+import sys
+from typing import Any, Sequence
+
+import numpy as np
+
+from . import _lib
+
+__all__ = ["CudaBatch", "CudaDeviceArrayView", "parse_fcs_state"]
+
+_TYPESTR_DTYPE = {"|u1": np.uint8, "<u1": np.uint8, "<f4": np.float32}
+_LEGACY_STREAM = 1  # cudaStreamLegacy
+
+
+def _torch():
+    return sys.modules.get("torch")
+
+
+def _current_stream(device: int) -> int:
+    torch = _torch()
+    if torch is not None and torch.cuda.is_available():
+        return torch.cuda.current_stream(device).cuda_stream or _LEGACY_STREAM
+    return _LEGACY_STREAM
+
+
+class CudaDeviceArrayView:
+    """Borrowed view of one device array of a CudaBatch (keeps the batch alive)."""
+
+    def __init__(self, owner: "CudaBatch", ptr: int, shape: tuple[int, ...], typestr: str, read_only: bool = False):
+        self._owner = owner
+        self._ptr = int(ptr)
+        self._shape = tuple(int(s) for s in shape)
+        self._typestr = typestr
+        self._read_only = read_only
+
+    @property
+    def __cuda_array_interface__(self) -> dict:  # cuda_module.cu:125-136
+        return {"shape": self._shape, "typestr": self._typestr, "data": (self._ptr, self._read_only),
+                "version": 3, "strides": None}
+
+    def __dlpack_device__(self) -> tuple[int, int]:
+        return (2, self._owner.device)  # kDLCUDA, real device ordinal
+
+    def __dlpack__(self, stream: Any = None, **_: Any):
+        """DLPack capsule; the consumer's `stream` is ordered after the batch's work."""
+        if stream != -1:
+            s = _LEGACY_STREAM if stream is None else int(stream)
+            self._owner._stream_wait(s)
+        torch = _torch()
+        if torch is None:
+            import torch  # noqa: F811  (DLPack export goes through torch)
+        t = torch.as_tensor(self, device=f"cuda:{self._owner.device}")
+        return torch.utils.dlpack.to_dlpack(t)
+
+    @property
+    def shape(self) -> tuple[int, ...]:
+        return self._shape
+
+
+def _fcs_dict(s: _lib.FcsState) -> dict:
+    out = {k: getattr(s, k) for k in ("pc", "a", "x", "y", "sp", "p", "cycles", "ppu_ctrl", "ppu_mask",
+                                      "ppu_status", "ppu_oam_addr", "ppu_open_bus", "ppu_read_buffer", "ppu_x",
+                                      "ppu_w", "ppu_v", "ppu_t")}
+    for k in ("cpu_ram", "prg_ram", "nametable_ram", "palette_ram", "oam"):
+        out[k] = bytes(getattr(s, k))
+    return out
+
+
+def parse_fcs_state(data: bytes) -> dict:
+    """Parse an already-decompressed FCEUX FCS save state into a dict of fields."""
+    lib = _lib.load()
+    raw = bytes(data)
+    buf = ctypes.create_string_buffer(raw, len(raw))
+    out = _lib.FcsState()
+    _lib.check(lib.nesle_parse_fcs(buf, len(raw), ctypes.byref(out)), lib)
+    return _fcs_dict(out)
+
+
+class CudaBatch:
+    """Batch of NROM consoles on one GPU (replaces CudaBatchBinding)."""
+
+    def __init__(self, num_envs: int, frameskip: int, rom_bytes: bytes | None = None,
+                 snapshot: bytes | Sequence[bytes] | None = None, env_to_level: Any = None, *,
+                 device: int | None = None, done_mode: int = _lib.DONE_SMB, done_args: tuple[int, int] = (0, 0),
+                 seed: int = 0, env_offset: int = 0, max_instructions_per_frame: int = 0):
+        self._lib = _lib.load()
+        self._h = None
+        if int(num_envs) <= 0:
+            raise ValueError("num_envs must be positive")
+        if int(frameskip) <= 0:
+            raise ValueError("frameskip must be positive")
+        if rom_bytes is None:
+            raise ValueError("the synthetic (ROM-less) CudaBatch mode is not provided by this build; pass rom_bytes")
+        snaps: list[bytes] = []
+        if snapshot is not None:
+            if isinstance(snapshot, (bytes, bytearray, memoryview)):
+                snaps = [bytes(snapshot)]
+                if env_to_level is not None:
+                    raise ValueError("env_to_level is only valid with a list of snapshots")
+            else:
+                snaps = [bytes(s) for s in snapshot]
+                if not snaps:
+                    raise ValueError("snapshot_bytes_list must contain at least one snapshot")
+                if len(snaps) > 255:
+                    raise ValueError("at most 255 snapshot levels supported per CudaBatch")
+                if env_to_level is None:
+                    raise ValueError("env_to_level must have shape (num_envs,)")
+                e2l = np.asarray(env_to_level)
+                if e2l.ndim != 1 or e2l.shape[0] != int(num_envs):
+                    raise ValueError("env_to_level must have shape (num_envs,)")
+                env_to_level = e2l.astype(np.uint8)
+        if device is None:
+            torch = _torch()
+            device = torch.cuda.current_device() if torch is not None and torch.cuda.is_available() else 0
+        self.device = int(device)
+        self.num_envs = int(num_envs)
+        self.frameskip = int(frameskip)
+        args, keep = _lib.make_create_args(self.num_envs, self.frameskip, bytes(rom_bytes), snaps, env_to_level,
+                                           done_mode, tuple(done_args), seed, env_offset, self.device,
+                                           max_instructions_per_frame)
+        h = ctypes.c_void_p()
+        _lib.check(self._lib.nesle_create(ctypes.byref(args), ctypes.byref(h)), self._lib)
+        self._h = h
+        self._num_levels = len(snaps)
+        self._faults_seen = 0
+        self._ptr_cache: dict[int, tuple[int, int]] = {}
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            self._lib.nesle_destroy(self._h)
+            self._h = None
+
+    # -- plumbing ---------------------------------------------------------
+    def _check(self, rc: int) -> None:
+        _lib.check(rc, self._lib)
+
+    def _stream(self) -> int:
+        return _current_stream(self.device)
+
+    def _stream_wait(self, stream: int) -> None:
+        self._check(self._lib.nesle_stream_wait(self._h, ctypes.c_void_p(stream)))
+
+    def synchronize(self) -> None:
+        self._check(self._lib.nesle_sync(self._h))
+        self._raise_on_fault()
+
+    def _raise_on_fault(self) -> None:
+        n = ctypes.c_uint32()
+        self._check(self._lib.nesle_fault_count(self._h, ctypes.byref(n)))
+        if n.value > self._faults_seen:
+            self._faults_seen = n.value
+            status = self._field("status")
+            bad = np.nonzero(status)[0]
+            if len(bad):
+                st = int(status[bad[0]])
+                raise RuntimeError(f"illegal 6502 opcode 0x{(st >> 16) & 0xFF:02x} at ${st & 0xFFFF:04x} "
+                                   f"in env {int(bad[0])} ({len(bad)} env(s) stopped)")
+
+    def _ptr(self, which: int) -> tuple[int, int]:
+        if which not in self._ptr_cache:
+            p, nb = ctypes.c_void_p(), ctypes.c_uint64()
+            self._check(self._lib.nesle_device_ptr(self._h, which, ctypes.byref(p), ctypes.byref(nb)))
+            self._ptr_cache[which] = (int(p.value), int(nb.value))
+        return self._ptr_cache[which]
+
+    def _field(self, name: str) -> np.ndarray:
+        dtype, shape = _lib.FIELDS[name]
+        out = np.empty((self.num_envs, *shape), dtype=dtype)
+        self._check(self._lib.nesle_copy_field(self._h, name.encode(), out.ctypes.data, out.nbytes))
+        return out
+
+    def _view(self, which: int, shape: tuple[int, ...], typestr: str) -> CudaDeviceArrayView:
+        ptr, _ = self._ptr(which)
+        return CudaDeviceArrayView(self, ptr, shape, typestr)
+
+    def _host_actions(self, actions: Any) -> np.ndarray:
+        a = np.ascontiguousarray(np.asarray(actions), dtype=np.uint8)
+        if a.ndim != 1 or a.shape[0] != self.num_envs:
+            raise ValueError("actions must have shape (num_envs,)")
+        return a
+
+    # -- reference API ----------------------------------------------------
+    def reset(self) -> np.ndarray:
+        """Reset every env; returns RGB frames (N, 240, 256, 3) (cuda_module.cu:469-516)."""
+        self._check(self._lib.nesle_reset(self._h, ctypes.c_void_p(self._stream())))
+        return self.render()
+
+    def reset_device(self) -> CudaDeviceArrayView:
+        self._check(self._lib.nesle_reset(self._h, ctypes.c_void_p(self._stream())))
+        self.synchronize()
+        return self.ram_device()
+
+    def step(self, actions: Any, render_frame: bool = True, copy_obs: bool = True) -> dict:
+        """Host-array step (cuda_module.cu:533-592): rewards/dones as numpy."""
+        a = self._host_actions(actions)
+        s = ctypes.c_void_p(self._stream())
+        self._check(self._lib.nesle_step(self._h, a.ctypes.data, _lib.ACTIONS_U8, 0, 0, 0, s))
+        if render_frame or copy_obs:
+            self._check(self._lib.nesle_render(self._h, _lib.RENDER_RGB, s))
+        self.synchronize()
+        out = {}
+        if copy_obs:
+            out["obs"] = self._copy_frames()
+        out["rewards"] = self._field("rewards")
+        out["dones"] = self._field("done")
+        return out
+
+    def step_device(self, actions: Any, auto_reset: bool = True, synchronize: bool = True) -> dict:
+        """Device-array step with fused auto-reset (cuda_module.cu:594-666)."""
+        ptr, dtype = self._device_actions(actions)
+        self._check(self._lib.nesle_step(self._h, ctypes.c_void_p(ptr), dtype, 1, 1, int(bool(auto_reset)),
+                                         ctypes.c_void_p(self._stream())))
+        if synchronize:
+            self.synchronize()
+        return {"rewards": self.rewards_device(), "dones": self.last_done_device(), "ram": self.ram_device()}
+
+    def step_stats(self, actions: Any) -> dict:
+        """step() plus per-env instruction/frame/budget counters (cuda_module.cu:668-732)."""
+        out = self.step(actions, render_frame=False, copy_obs=False)
+        out["instructions"] = self._field("stat_instructions")
+        out["frames_completed"] = self._field("stat_frames")
+        out["budget_hits"] = self._field("stat_budget_hits")
+        return out
+
+    def render(self) -> np.ndarray:
+        self.render_device()
+        self.synchronize()
+        return self._copy_frames()
+
+    def render_device(self) -> None:
+        self._check(self._lib.nesle_render(self._h, _lib.RENDER_RGB, ctypes.c_void_p(self._stream())))
+
+    def ram(self) -> np.ndarray:
+        return self._field("ram")
+
+    def ram_device(self) -> CudaDeviceArrayView:
+        return self._view(_lib.PTR_RAM, (self.num_envs, 2048), "|u1")
+
+    def frames_device(self) -> CudaDeviceArrayView:
+        return self._view(_lib.PTR_FRAMES_RGB, (self.num_envs, 240, 256, 3), "|u1")
+
+    def rewards_device(self) -> CudaDeviceArrayView:
+        return self._view(_lib.PTR_LAST_REWARDS, (self.num_envs,), "<f4")
+
+    def last_done_device(self) -> CudaDeviceArrayView:
+        return self._view(_lib.PTR_LAST_DONE, (self.num_envs,), "|u1")
+
+    def oam(self) -> np.ndarray:
+        return self._field("oam")
+
+    def reset_envs(self, mask: Any) -> None:
+        m = np.ascontiguousarray(np.asarray(mask), dtype=np.uint8)
+        if m.ndim != 1 or m.shape[0] != self.num_envs:
+            raise ValueError("mask must have shape (num_envs,)")
+        self._check(self._lib.nesle_reset_envs(self._h, m.ctypes.data, 0, ctypes.c_void_p(self._stream())))
+        self.synchronize()
+
+    def poke_ram(self, address: int, value: int) -> None:
+        self._check(self._lib.nesle_poke_ram(self._h, int(address) & 0xFFFF, int(value) & 0xFF,
+                                             ctypes.c_void_p(self._stream())))
+        self.synchronize()
+
+    @property
+    def name(self) -> str:
+        return "cuda-console"
+
+    @property
+    def has_snapshot(self) -> bool:
+        return self._num_levels > 0
+
+    @property
+    def num_levels(self) -> int:
+        return self._num_levels
+
+    # -- extensions -------------------------------------------------------
+    def frames_index_device(self, render: bool = True) -> CudaDeviceArrayView:
+        if render:
+            self._check(self._lib.nesle_render(self._h, _lib.RENDER_INDEX, ctypes.c_void_p(self._stream())))
+        return self._view(_lib.PTR_FRAMES_INDEX, (self.num_envs, 240, 256), "|u1")
+
+    def obs_gray84_device(self, render: bool = True) -> CudaDeviceArrayView:
+        if render:
+            self._check(self._lib.nesle_render(self._h, _lib.RENDER_GRAY84, ctypes.c_void_p(self._stream())))
+        return self._view(_lib.PTR_OBS_GRAY84, (self.num_envs, 84, 84), "|u1")
+
+    def get_field(self, name: str) -> np.ndarray:
+        """Host copy of any per-env field of the C ABI (nesle_copy_field)."""
+        return self._field(name)
+
+    # -- helpers ----------------------------------------------------------
+    def _copy_frames(self) -> np.ndarray:
+        return self._field("frames_rgb")
+
+    def _device_actions(self, actions: Any) -> tuple[int, int]:
+        """(pointer, dtype code) of CUDA actions (cuda_module.cu:259-308)."""
+        if hasattr(actions, "data_ptr") and hasattr(actions, "is_cuda"):
+            if not actions.is_cuda:
+                raise ValueError("expected CUDA actions, got a CPU tensor")
+            if hasattr(actions, "is_contiguous") and not actions.is_contiguous():
+                raise ValueError("CUDA action tensor must be contiguous")
+            if tuple(actions.shape) != (self.num_envs,):
+                raise ValueError(f"CUDA action tensor must have shape ({self.num_envs},)")
+            dt = str(actions.dtype)
+            if dt == "torch.uint8":
+                code = _lib.ACTIONS_U8
+            elif dt == "torch.int64":
+                code = _lib.ACTIONS_I64
+            else:
+                raise ValueError("CUDA actions must have dtype torch.uint8 or torch.int64")
+            if actions.device.index is not None and actions.device.index != self.device:
+                raise ValueError(f"CUDA actions live on device {actions.device.index}, batch on {self.device}")
+            return int(actions.data_ptr()), code
+        if not hasattr(actions, "__cuda_array_interface__"):
+            raise ValueError("expected a CUDA tensor/array exposing __cuda_array_interface__")
+        iface = actions.__cuda_array_interface__
+        if tuple(iface["shape"]) != (self.num_envs,):
+            raise ValueError(f"CUDA action array must have shape ({self.num_envs},)")
+        ts = iface["typestr"]
+        if ts in ("|u1", "<u1"):
+            code = _lib.ACTIONS_U8
+        elif ts in ("<i8", "|i8"):
+            code = _lib.ACTIONS_I64
+        else:
+            raise ValueError("CUDA actions must be uint8 masks or int64 values already encoded as masks")
+        return int(iface["data"][0]), code

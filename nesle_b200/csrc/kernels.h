@@ -1,0 +1,23 @@
+// kernels.h -- host-side launchers of the batched NES kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "nesle_state.h"
+
+namespace nesle {
+
+constexpr uint32_t kStepSlots = 96;  // envs (threads) per step CTA
+
+enum : uint32_t { kStepDeviceApi = 1, kStepAutoReset = 2 };
+
+size_t step_smem_bytes();
+cudaError_t configure_kernels();
+cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* act8, const long long* act64,
+                        uint32_t flags, cudaStream_t s);
+cudaError_t launch_reset(const BatchView* dv, uint32_t num_envs, const uint8_t* mask, bool full, cudaStream_t s);
+cudaError_t launch_poke(const BatchView* dv, uint32_t num_envs, uint32_t address, uint32_t value, cudaStream_t s);
+cudaError_t launch_render(const BatchView* dv, uint32_t num_envs, uint8_t* out, int mode, cudaStream_t s);
+
+}  // namespace nesle

@@ -1,0 +1,1027 @@
+// nes_core.cuh -- the per-env NES core of the B200 env-step kernel.
+//
+// One CUDA thread runs one console.  The hot loop is a *uniform datapath*
+// 6502: every opcode executes the same instruction stream (fetch, table
+// decode, effective address, one memory read, a combined adder/logic/shifter,
+// one memory write, register/flag write-back), with the differences between
+// opcodes carried as data in a 64-bit decode word.  Lanes of a warp that sit at
+// different PCs therefore stay converged through the common path; only I/O
+// accesses, NMI entry, PPU event settlement, OAM DMA and the stack-transfer
+// instructions (JSR/RTS/RTI/BRK/JMP-indirect) take divergent side paths.
+//
+// Semantics restate the reference batched kernel (hbofz/NeSLE
+// cpp/src/cuda/kernels.cu:19-104 and cpp/include/nesle/cpu.hpp,
+// cuda/batch_bus.cuh, cuda/batch_ppu.cuh, cuda/batch_console.hpp,
+// cuda/batch_step.cuh); each function names the lines it follows.
+//
+// Memory: the env's 2 KB RAM lives in shared memory in a bank-interleaved
+// layout -- byte `a` of the env in slot `s` of a CTA with `S` slots is at
+// ((a & 0x7FC) * S + s * 4 + (a & 3)) -- so slot s always hits bank s % 32 and
+// no RAM access of a warp ever bank-conflicts.  PRG ROM (32 KB) and the decode
+// table are staged once per CTA into shared memory as well.
+//
+// The header also compiles as plain C++ (NESLE_HD expands to nothing) so the
+// same code can be unit-tested on the CPU against the checker.
+#pragma once
+#include <stdint.h>
+#include <string.h>
+
+#include "nesle_state.h"
+
+#ifdef __CUDACC__
+#define NESLE_HD __host__ __device__ __forceinline__
+#else
+#define NESLE_HD inline
+#endif
+
+namespace nesle {
+
+// ---------------------------------------------------------------------------
+// Decode word.
+// ---------------------------------------------------------------------------
+enum Mode : uint32_t { IMP, ACC, IMM, ZP, ZPX, ZPY, ABS, ABSX, ABSY, INDX, INDY, IND, REL, PUSH, PULL };
+
+// bit positions
+enum : uint32_t {
+    D_LEN = 4,       // 2 bits: length - 1
+    D_IDX = 6,       // 2 bits: 0 none, 1 X, 2 Y
+    D_BASE = 8,      // 2 bits: 0 b1 (zero page), 1 b1|b2<<8, 2 indirect, 3 stack
+    D_ZPW = 10,      // zero-page wrap
+    D_INDX = 11,     // (zp,X): add X to the pointer
+    D_IMM = 12,      // operand value is the immediate byte
+    D_PULL = 13,     // stack address pre-increments
+    D_CYC = 14,      // 3 bits: base cycles
+    D_PAGE = 17,     // +1 cycle on page cross
+    D_RD = 18,       // reads the memory operand
+    D_WM = 19,       // writes the result to memory
+    D_OPA = 20,      // 3 bits: 0 A, 1 X, 2 Y, 3 SP, 4 M, 5 zero, 6 P|$30
+    D_BM = 23,       // adder B input uses M
+    D_BX = 24,       // adder B input xor $FF
+    D_CINC = 25,     // adder carry-in = C
+    D_CIN1 = 26,     // adder carry-in = 1
+    D_UNIT = 27,     // 3 bits: 0 add, 1 and, 2 or, 3 xor, 4 shl, 5 shr
+    D_ROT = 30,      // shift rotates through C
+    D_WA = 31,       // write A
+    D_WX = 32,
+    D_WY = 33,
+    D_WSP = 34,
+    D_WP = 35,       // PLP: P <- (r | $20) & ~$10
+    D_SPD = 36,      // 2 bits: 0 none, 1 SP-1, 2 SP+1
+    D_FLG = 38,      // 2 bits: 0 none, 1 NZ, 2 NZC, 3 NZCV
+    D_BIT = 40,      // BIT: N,V from M, Z from r
+    D_FCM = 41,      // 8 bits: constant flag mask (CLC/SEC/...)
+    D_FCV = 49,      // constant flag value (set when 1)
+    D_BR = 50,       // branch
+    D_BRF = 51,      // 3 bits: flag bit position tested
+    D_BRP = 54,      // branch taken when flag == this
+    D_JMP = 55,      // JMP absolute
+    D_SPECIAL = 56,  // JSR RTS RTI BRK JMP(ind): side path
+    D_ILLEGAL = 57,
+};
+
+enum : uint32_t { U_ADD, U_AND, U_OR, U_XOR, U_SHL, U_SHR };
+enum : uint32_t { A_A, A_X, A_Y, A_SP, A_M, A_ZERO, A_PHP };
+enum : uint32_t { F_NONE, F_NZ, F_NZC, F_NZCV };
+
+struct DecodeTable {
+    uint64_t e[256];
+};
+
+namespace dt {
+constexpr uint64_t B(uint32_t pos, uint64_t v = 1) { return v << pos; }
+
+constexpr uint64_t mode_bits(Mode m) {
+    uint64_t len = 0, idx = 0, base = 0, zpw = 0, indx = 0, imm = 0, pull = 0;
+    switch (m) {
+        case IMP: case ACC: len = 0; break;
+        case IMM: len = 1; imm = 1; break;
+        case ZP: len = 1; base = 0; zpw = 1; break;
+        case ZPX: len = 1; base = 0; zpw = 1; idx = 1; break;
+        case ZPY: len = 1; base = 0; zpw = 1; idx = 2; break;
+        case ABS: len = 2; base = 1; break;
+        case ABSX: len = 2; base = 1; idx = 1; break;
+        case ABSY: len = 2; base = 1; idx = 2; break;
+        case INDX: len = 1; base = 2; indx = 1; break;
+        case INDY: len = 1; base = 2; idx = 2; break;
+        case IND: len = 2; base = 1; break;
+        case REL: len = 1; break;
+        case PUSH: len = 0; base = 3; break;
+        case PULL: len = 0; base = 3; pull = 1; break;
+    }
+    return uint64_t(m) | B(D_LEN, len) | B(D_IDX, idx) | B(D_BASE, base) | B(D_ZPW, zpw) |
+           B(D_INDX, indx) | B(D_IMM, imm) | B(D_PULL, pull);
+}
+
+struct Op {
+    uint32_t opa = A_ZERO, unit = U_ADD;
+    bool bm = false, bx = false, cinc = false, cin1 = false, rot = false;
+    bool rd = false, wm = false, wa = false, wx = false, wy = false, wsp = false, wp = false;
+    uint32_t spd = 0, flg = F_NONE;
+    bool bit = false;
+    uint32_t fcm = 0;
+    bool fcv = false, br = false, jmp = false, special = false;
+    uint32_t brf = 0;
+    bool brp = false;
+};
+
+constexpr uint64_t pack(Mode m, uint32_t cycles, bool page, const Op& o) {
+    uint64_t w = mode_bits(m) | B(D_CYC, cycles) | B(D_PAGE, page ? 1 : 0);
+    w |= B(D_RD, o.rd) | B(D_WM, o.wm) | B(D_OPA, o.opa) | B(D_BM, o.bm) | B(D_BX, o.bx);
+    w |= B(D_CINC, o.cinc) | B(D_CIN1, o.cin1) | B(D_UNIT, o.unit) | B(D_ROT, o.rot);
+    w |= B(D_WA, o.wa) | B(D_WX, o.wx) | B(D_WY, o.wy) | B(D_WSP, o.wsp) | B(D_WP, o.wp);
+    w |= B(D_SPD, o.spd) | B(D_FLG, o.flg) | B(D_BIT, o.bit) | B(D_FCM, o.fcm) | B(D_FCV, o.fcv);
+    w |= B(D_BR, o.br) | B(D_BRF, o.brf) | B(D_BRP, o.brp) | B(D_JMP, o.jmp) | B(D_SPECIAL, o.special);
+    return w;
+}
+
+// Operation templates.
+constexpr Op load(uint32_t dst) {  // LDA/LDX/LDY: r = M
+    Op o; o.rd = true; o.opa = A_ZERO; o.bm = true; o.flg = F_NZ;
+    o.wa = dst == 0; o.wx = dst == 1; o.wy = dst == 2; return o;
+}
+constexpr Op store(uint32_t src) {  // STA/STX/STY: mem <- reg
+    Op o; o.wm = true; o.opa = src; return o;
+}
+constexpr Op logic(uint32_t unit) { Op o; o.rd = true; o.opa = A_A; o.unit = unit; o.wa = true; o.flg = F_NZ; return o; }
+constexpr Op adc(bool sub) {
+    Op o; o.rd = true; o.opa = A_A; o.bm = true; o.bx = sub; o.cinc = true; o.wa = true; o.flg = F_NZCV; return o;
+}
+constexpr Op cmp(uint32_t reg) { Op o; o.rd = true; o.opa = reg; o.bm = true; o.bx = true; o.cin1 = true; o.flg = F_NZC; return o; }
+constexpr Op bit() { Op o; o.rd = true; o.opa = A_A; o.unit = U_AND; o.bit = true; return o; }
+constexpr Op incdec_mem(bool dec) {
+    Op o; o.rd = true; o.wm = true; o.opa = A_M; o.bx = dec; o.cin1 = !dec; o.flg = F_NZ; return o;
+}
+constexpr Op incdec_reg(uint32_t reg, bool dec) {
+    Op o; o.opa = reg; o.bx = dec; o.cin1 = !dec; o.flg = F_NZ; o.wx = reg == A_X; o.wy = reg == A_Y; return o;
+}
+constexpr Op shift(bool right, bool rot, bool acc) {
+    Op o; o.unit = right ? U_SHR : U_SHL; o.rot = rot; o.flg = F_NZC;
+    if (acc) { o.opa = A_A; o.wa = true; } else { o.opa = A_M; o.rd = true; o.wm = true; }
+    return o;
+}
+constexpr Op transfer(uint32_t src, uint32_t dst, bool flags) {
+    Op o; o.opa = src; o.flg = flags ? F_NZ : F_NONE;
+    o.wa = dst == A_A; o.wx = dst == A_X; o.wy = dst == A_Y; o.wsp = dst == A_SP; return o;
+}
+constexpr Op flagop(uint32_t mask, bool set) { Op o; o.fcm = mask; o.fcv = set; return o; }
+constexpr Op branch(uint32_t flagpos, bool pol) { Op o; o.br = true; o.brf = flagpos; o.brp = pol; return o; }
+
+constexpr DecodeTable build() {
+    DecodeTable t{};
+    for (auto& e : t.e) e = B(D_ILLEGAL);
+    // group-1 ALU ops: opcode base + {imm 09, zp 05, zpx 15, abs 0D, absx 1D, absy 19, indx 01, indy 11}
+    struct G1 { uint32_t base; Op op; };
+    const G1 g1[] = {{0x00, logic(U_OR)}, {0x20, logic(U_AND)}, {0x40, logic(U_XOR)}, {0x60, adc(false)},
+                     {0xA0, load(0)}, {0xC0, cmp(A_A)}, {0xE0, adc(true)}};
+    for (const auto& g : g1) {
+        t.e[g.base + 0x09] = pack(IMM, 2, false, g.op);
+        t.e[g.base + 0x05] = pack(ZP, 3, false, g.op);
+        t.e[g.base + 0x15] = pack(ZPX, 4, false, g.op);
+        t.e[g.base + 0x0D] = pack(ABS, 4, false, g.op);
+        t.e[g.base + 0x1D] = pack(ABSX, 4, true, g.op);
+        t.e[g.base + 0x19] = pack(ABSY, 4, true, g.op);
+        t.e[g.base + 0x01] = pack(INDX, 6, false, g.op);
+        t.e[g.base + 0x11] = pack(INDY, 5, true, g.op);
+    }
+    // The immediate forms of the logic ops read b1 (D_IMM); clear D_RD there.
+    for (uint32_t b : {0x09u, 0x29u, 0x49u, 0x69u, 0xA9u, 0xC9u, 0xE9u}) t.e[b] &= ~B(D_RD);
+    const Op sta = store(A_A);
+    t.e[0x85] = pack(ZP, 3, false, sta); t.e[0x95] = pack(ZPX, 4, false, sta);
+    t.e[0x8D] = pack(ABS, 4, false, sta); t.e[0x9D] = pack(ABSX, 5, false, sta);
+    t.e[0x99] = pack(ABSY, 5, false, sta); t.e[0x81] = pack(INDX, 6, false, sta);
+    t.e[0x91] = pack(INDY, 6, false, sta);
+    // shifts: acc 0A, zp 06, zpx 16, abs 0E, absx 1E
+    struct SH { uint32_t base; bool right, rot; };
+    const SH sh[] = {{0x00, false, false}, {0x20, false, true}, {0x40, true, false}, {0x60, true, true}};
+    for (const auto& s : sh) {
+        t.e[s.base + 0x0A] = pack(ACC, 2, false, shift(s.right, s.rot, true));
+        t.e[s.base + 0x06] = pack(ZP, 5, false, shift(s.right, s.rot, false));
+        t.e[s.base + 0x16] = pack(ZPX, 6, false, shift(s.right, s.rot, false));
+        t.e[s.base + 0x0E] = pack(ABS, 6, false, shift(s.right, s.rot, false));
+        t.e[s.base + 0x1E] = pack(ABSX, 7, false, shift(s.right, s.rot, false));
+    }
+    const Op inc = incdec_mem(false), dec = incdec_mem(true);
+    t.e[0xE6] = pack(ZP, 5, false, inc); t.e[0xF6] = pack(ZPX, 6, false, inc);
+    t.e[0xEE] = pack(ABS, 6, false, inc); t.e[0xFE] = pack(ABSX, 7, false, inc);
+    t.e[0xC6] = pack(ZP, 5, false, dec); t.e[0xD6] = pack(ZPX, 6, false, dec);
+    t.e[0xCE] = pack(ABS, 6, false, dec); t.e[0xDE] = pack(ABSX, 7, false, dec);
+    const Op ldx = load(1), ldy = load(2);
+    t.e[0xA2] = pack(IMM, 2, false, ldx) & ~B(D_RD); t.e[0xA6] = pack(ZP, 3, false, ldx);
+    t.e[0xB6] = pack(ZPY, 4, false, ldx); t.e[0xAE] = pack(ABS, 4, false, ldx);
+    t.e[0xBE] = pack(ABSY, 4, true, ldx);
+    t.e[0xA0] = pack(IMM, 2, false, ldy) & ~B(D_RD); t.e[0xA4] = pack(ZP, 3, false, ldy);
+    t.e[0xB4] = pack(ZPX, 4, false, ldy); t.e[0xAC] = pack(ABS, 4, false, ldy);
+    t.e[0xBC] = pack(ABSX, 4, true, ldy);
+    const Op stx = store(A_X), sty = store(A_Y);
+    t.e[0x86] = pack(ZP, 3, false, stx); t.e[0x96] = pack(ZPY, 4, false, stx); t.e[0x8E] = pack(ABS, 4, false, stx);
+    t.e[0x84] = pack(ZP, 3, false, sty); t.e[0x94] = pack(ZPX, 4, false, sty); t.e[0x8C] = pack(ABS, 4, false, sty);
+    const Op cpx = cmp(A_X), cpy = cmp(A_Y);
+    t.e[0xE0] = pack(IMM, 2, false, cpx) & ~B(D_RD); t.e[0xE4] = pack(ZP, 3, false, cpx);
+    t.e[0xEC] = pack(ABS, 4, false, cpx);
+    t.e[0xC0] = pack(IMM, 2, false, cpy) & ~B(D_RD); t.e[0xC4] = pack(ZP, 3, false, cpy);
+    t.e[0xCC] = pack(ABS, 4, false, cpy);
+    t.e[0x24] = pack(ZP, 3, false, bit()); t.e[0x2C] = pack(ABS, 4, false, bit());
+    Op jmp; jmp.jmp = true;
+    t.e[0x4C] = pack(ABS, 3, false, jmp);
+    Op special; special.special = true;
+    t.e[0x6C] = pack(IND, 5, false, special);
+    t.e[0x20] = pack(ABS, 6, false, special);
+    t.e[0x60] = pack(IMP, 6, false, special);
+    t.e[0x40] = pack(IMP, 6, false, special);
+    t.e[0x00] = pack(IMP, 7, false, special);
+    // branches: xxy10000, bits 7-6 select N V C Z, bit 5 the value that branches
+    const uint32_t flagpos[4] = {7, 6, 0, 1};
+    for (uint32_t op = 0x10; op <= 0xF0; op += 0x20)
+        t.e[op] = pack(REL, 2, false, branch(flagpos[op >> 6], (op & 0x20) != 0));
+    // stack
+    Op pha = store(A_A); pha.spd = 1;
+    Op php = store(A_PHP); php.spd = 1;
+    Op pla = load(0); pla.spd = 2;
+    Op plp; plp.rd = true; plp.opa = A_ZERO; plp.bm = true; plp.wp = true; plp.spd = 2;
+    t.e[0x48] = pack(PUSH, 3, false, pha); t.e[0x08] = pack(PUSH, 3, false, php);
+    t.e[0x68] = pack(PULL, 4, false, pla); t.e[0x28] = pack(PULL, 4, false, plp);
+    // flags: C=01 I=04 D=08 V=40
+    t.e[0x18] = pack(IMP, 2, false, flagop(0x01, false)); t.e[0x38] = pack(IMP, 2, false, flagop(0x01, true));
+    t.e[0x58] = pack(IMP, 2, false, flagop(0x04, false)); t.e[0x78] = pack(IMP, 2, false, flagop(0x04, true));
+    t.e[0xB8] = pack(IMP, 2, false, flagop(0x40, false)); t.e[0xD8] = pack(IMP, 2, false, flagop(0x08, false));
+    t.e[0xF8] = pack(IMP, 2, false, flagop(0x08, true));
+    // register ops
+    t.e[0xE8] = pack(IMP, 2, false, incdec_reg(A_X, false)); t.e[0xCA] = pack(IMP, 2, false, incdec_reg(A_X, true));
+    t.e[0xC8] = pack(IMP, 2, false, incdec_reg(A_Y, false)); t.e[0x88] = pack(IMP, 2, false, incdec_reg(A_Y, true));
+    t.e[0xAA] = pack(IMP, 2, false, transfer(A_A, A_X, true)); t.e[0xA8] = pack(IMP, 2, false, transfer(A_A, A_Y, true));
+    t.e[0x8A] = pack(IMP, 2, false, transfer(A_X, A_A, true)); t.e[0x98] = pack(IMP, 2, false, transfer(A_Y, A_A, true));
+    t.e[0xBA] = pack(IMP, 2, false, transfer(A_SP, A_X, true)); t.e[0x9A] = pack(IMP, 2, false, transfer(A_X, A_SP, false));
+    t.e[0xEA] = pack(IMP, 2, false, Op{});
+    return t;
+}
+}  // namespace dt
+
+constexpr DecodeTable kDecodeHost = dt::build();
+
+NESLE_HD uint32_t dfield(uint64_t d, uint32_t pos, uint32_t bits) {
+    return static_cast<uint32_t>(d >> pos) & ((1u << bits) - 1u);
+}
+
+// ---------------------------------------------------------------------------
+// Counter RNG (SplitMix64 finaliser, Steele/Lea/Flood 2014), keyed exactly as
+// nesle_b200.workloads.counter_rand.
+// ---------------------------------------------------------------------------
+NESLE_HD uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+NESLE_HD uint32_t frame_limit(const BatchView& v, uint32_t env, uint32_t episode) {
+    uint64_t k = splitmix64(v.seed ^ (2ull << 56));
+    k = splitmix64(k ^ (uint64_t)(v.env_offset + env));
+    k = splitmix64(k ^ (uint64_t)episode);
+    return v.done_a + (uint32_t)(k % (uint64_t)(v.done_b - v.done_a + 1));
+}
+
+// ---------------------------------------------------------------------------
+// Lane state: every scalar of the env, register-resident during a launch.
+// ---------------------------------------------------------------------------
+struct Lane {
+    uint32_t pc, a, x, y, sp, p;
+    uint64_t cycles;
+    uint64_t frame;
+    uint32_t frame_dot, ctrl, mask, status, nmi;
+    uint32_t oam_addr, v, t, fine_x, w, open_bus, read_buffer, scroll_x, scroll_y;
+    uint32_t lat_sx, lat_sy, lat_ctrl, ssx0, ssy0, sc0, ssx1, ssy1, sc1, smask;
+    uint32_t cshift, ccount, cstrobe, action, flags;
+    int32_t prev_x, prev_time;
+    uint32_t episode, status_word, cpu_nmi, irq;
+    uint32_t dma;  // pending OAM-DMA cycles of the current instruction
+    // per-launch loop state
+    uint32_t pending, horizon, instr, fcomp, fidx;
+    uint64_t tot_instr;
+    uint32_t tot_frames, budget;
+};
+
+NESLE_HD void load_lane(Lane& L, const EnvRecord& r, uint8_t action) {
+    L.pc = r.pc; L.a = r.a; L.x = r.x; L.y = r.y; L.sp = r.sp; L.p = r.p;
+    L.cycles = r.cycles; L.frame = r.frame; L.frame_dot = r.frame_dot;
+    L.ctrl = r.ppu_ctrl; L.mask = r.ppu_mask; L.status = r.ppu_status; L.nmi = r.nmi_pending;
+    L.oam_addr = r.oam_addr; L.v = r.v; L.t = r.t; L.fine_x = r.fine_x; L.w = r.w;
+    L.open_bus = r.open_bus; L.read_buffer = r.read_buffer; L.scroll_x = r.scroll_x; L.scroll_y = r.scroll_y;
+    L.lat_sx = r.lat_sx; L.lat_sy = r.lat_sy; L.lat_ctrl = r.lat_ctrl;
+    L.ssx0 = r.snap_sx_start; L.ssy0 = r.snap_sy_start; L.sc0 = r.snap_ctrl_start;
+    L.ssx1 = r.snap_sx_end; L.ssy1 = r.snap_sy_end; L.sc1 = r.snap_ctrl_end; L.smask = r.snap_mask;
+    L.cshift = r.ctrl_shift; L.ccount = r.ctrl_count; L.cstrobe = r.ctrl_strobe; L.flags = r.flags;
+    L.action = action;
+    L.prev_x = r.prev_x; L.prev_time = r.prev_time; L.episode = r.episode; L.status_word = r.status;
+    L.cpu_nmi = r.cpu_nmi_pending; L.irq = r.irq_pending; L.dma = r.pending_dma;
+}
+
+NESLE_HD void store_lane(const Lane& L, EnvRecord& r) {
+    r.pc = (uint16_t)L.pc; r.a = (uint8_t)L.a; r.x = (uint8_t)L.x; r.y = (uint8_t)L.y;
+    r.sp = (uint8_t)L.sp; r.p = (uint8_t)L.p; r.nmi_pending = (uint8_t)L.nmi;
+    r.cycles = L.cycles; r.frame = L.frame; r.frame_dot = L.frame_dot;
+    r.ppu_ctrl = (uint8_t)L.ctrl; r.ppu_mask = (uint8_t)L.mask; r.ppu_status = (uint8_t)L.status;
+    r.oam_addr = (uint8_t)L.oam_addr; r.v = (uint16_t)L.v; r.t = (uint16_t)L.t;
+    r.fine_x = (uint8_t)L.fine_x; r.w = (uint8_t)L.w; r.open_bus = (uint8_t)L.open_bus;
+    r.read_buffer = (uint8_t)L.read_buffer; r.scroll_x = (uint8_t)L.scroll_x; r.scroll_y = (uint8_t)L.scroll_y;
+    r.lat_sx = (uint8_t)L.lat_sx; r.lat_sy = (uint8_t)L.lat_sy; r.lat_ctrl = (uint8_t)L.lat_ctrl;
+    r.snap_sx_start = (uint8_t)L.ssx0; r.snap_sy_start = (uint8_t)L.ssy0; r.snap_ctrl_start = (uint8_t)L.sc0;
+    r.snap_sx_end = (uint8_t)L.ssx1; r.snap_sy_end = (uint8_t)L.ssy1; r.snap_ctrl_end = (uint8_t)L.sc1;
+    r.snap_mask = (uint8_t)L.smask;
+    r.ctrl_shift = (uint8_t)L.cshift; r.ctrl_count = (uint8_t)L.ccount; r.ctrl_strobe = (uint8_t)L.cstrobe;
+    r.flags = (uint8_t)L.flags; r.prev_x = L.prev_x; r.prev_time = L.prev_time;
+    r.pending_dma = L.dma; r.episode = L.episode; r.status = L.status_word;
+    r.cpu_nmi_pending = (uint8_t)L.cpu_nmi; r.irq_pending = (uint8_t)L.irq;
+    r.stat_instructions = L.tot_instr; r.stat_frames = L.tot_frames; r.stat_budget_hits = L.budget;
+}
+
+// ---------------------------------------------------------------------------
+// Memory context of one lane: RAM slot in the interleaved shared array, the
+// shared PRG/decode copies, and the env's rows of the global byte arrays.
+// ---------------------------------------------------------------------------
+struct Ctx {
+    uint8_t* ram;         // &smem_ram[slot * 4]; byte a at ram[(a & 0x7FC) * slots + (a & 3)]
+    uint32_t slots;       // RAM slots per CTA (interleave stride / 4)
+    const uint8_t* prg;   // 32 KB (shared)
+    const uint64_t* dec;  // decode table (shared)
+    const BatchView* view;
+    uint32_t env;
+    uint32_t frameskip;   // copies of view fields read on every iteration
+    uint32_t max_instr;
+    uint8_t* prg_ram;     // env rows in global memory
+    uint8_t* nt;
+    uint8_t* pal;
+    uint8_t* oam;
+};
+
+NESLE_HD uint32_t ram_off(const Ctx& c, uint32_t a) { return (a & 0x7FCu) * c.slots + (a & 3u); }
+NESLE_HD uint32_t ram_rd(const Ctx& c, uint32_t a) { return c.ram[ram_off(c, a)]; }
+NESLE_HD void ram_wr(const Ctx& c, uint32_t a, uint32_t v) { c.ram[ram_off(c, a)] = (uint8_t)v; }
+
+// 16-byte-aligned row copies (every row base is a multiple of 16).
+NESLE_HD void copy16(uint8_t* dst, const uint8_t* src) {
+#if defined(__CUDA_ARCH__)
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+#else
+    memcpy(dst, src, 16);
+#endif
+}
+NESLE_HD void store16(uint8_t* dst, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+#if defined(__CUDA_ARCH__)
+    *reinterpret_cast<uint4*>(dst) = make_uint4(a, b, c, d);
+#else
+    const uint32_t w[4] = {a, b, c, d};
+    memcpy(dst, w, 16);
+#endif
+}
+NESLE_HD void zero_row(uint8_t* dst, uint32_t n) {
+    for (uint32_t i = 0; i < n; i += 16) store16(dst + i, 0, 0, 0, 0);
+}
+NESLE_HD void copy_row(uint8_t* dst, const uint8_t* src, uint32_t n) {
+    for (uint32_t i = 0; i < n; i += 16) copy16(dst + i, src + i);
+}
+
+// ---------------------------------------------------------------------------
+// PPU memory and registers: batch_bus.cuh:35-103, 156-292.
+// ---------------------------------------------------------------------------
+NESLE_HD uint32_t mirror_pal(uint32_t a) {
+    uint32_t i = a & 0x1F;
+    return ((i & 0x13) == 0x10) ? i - 0x10 : i;  // $10/$14/$18/$1C alias $00/$04/$08/$0C
+}
+NESLE_HD uint32_t mirror_nt(uint32_t horizontal, uint32_t a) {
+    uint32_t i = (a - 0x2000u) & 0x0FFFu;
+    return horizontal ? ((i & 0x03FFu) | ((i & 0x0800u) >> 1)) : (i & 0x07FFu);
+}
+NESLE_HD uint32_t ppu_mem_rd(const Ctx& c, uint32_t a) {
+    a &= 0x3FFF;
+    if (a < 0x2000) return c.view->chr_size ? c.view->chr[a % c.view->chr_size] : 0u;
+    if (a < 0x3F00) {
+        if (a >= 0x3000) a -= 0x1000;
+        return c.nt[mirror_nt(c.view->horizontal, a)];
+    }
+    return c.pal[mirror_pal(a)];
+}
+NESLE_HD void ppu_mem_wr(const Ctx& c, Lane& L, uint32_t a, uint32_t v) {
+    a &= 0x3FFF;
+    if (a < 0x2000) return;
+    if (a < 0x3F00) {
+        if (a >= 0x3000) a -= 0x1000;
+        c.nt[mirror_nt(c.view->horizontal, a)] = (uint8_t)v;
+        L.flags |= kFlagNtDirty;
+        return;
+    }
+    c.pal[mirror_pal(a)] = (uint8_t)v;
+    L.flags |= kFlagPalDirty;
+}
+
+// batch_bus.cuh:135-154: OAM DMA from RAM page & 0x7FF, +513 cycles.
+NESLE_HD void oam_dma(const Ctx& c, Lane& L, uint32_t page) {
+    const uint32_t base = (page << 8) & 0x7FF;
+    if ((L.oam_addr & 0xFF) == 0) {
+        // Aligned destination: assemble 4 RAM bytes (one interleaved smem word
+        // each) and store 16 bytes at a time.
+        for (uint32_t i = 0; i < 256; i += 16) {
+            uint32_t wds[4];
+            for (uint32_t k = 0; k < 4; ++k) {
+                const uint32_t a = base + i + 4 * k;
+                const uint8_t* src = c.ram + (a & 0x7FCu) * c.slots;
+                wds[k] = (uint32_t)src[0] | ((uint32_t)src[1] << 8) | ((uint32_t)src[2] << 16) |
+                         ((uint32_t)src[3] << 24);
+            }
+            store16(c.oam + i, wds[0], wds[1], wds[2], wds[3]);
+        }
+    } else {
+        for (uint32_t i = 0; i < 256; ++i) c.oam[(L.oam_addr + i) & 0xFF] = (uint8_t)ram_rd(c, base + i);
+    }
+    L.flags |= kFlagOamDirty;
+    L.dma += 513;
+}
+
+// Side-effecting or non-RAM/PRG read: batch_bus.cuh:156-213.
+NESLE_HD uint32_t io_rd(const Ctx& c, Lane& L, uint32_t a) {
+    if (a < 0x2000) return ram_rd(c, a);
+    if (a < 0x4000) {
+        const uint32_t reg = a & 7;
+        if (reg == 2) {
+            const uint32_t val = (L.status & 0xE0) | (L.open_bus & 0x1F);
+            L.status &= 0x7F;
+            L.nmi = 0;
+            L.w = 0;
+            L.open_bus = val;
+            return val;
+        }
+        if (reg == 4) return c.oam[L.oam_addr & 0xFF];
+        if (reg == 7) {
+            const uint32_t pa = L.v & 0x3FFF;
+            uint32_t val;
+            if (pa >= 0x3F00) {
+                val = ppu_mem_rd(c, pa);
+                L.read_buffer = ppu_mem_rd(c, pa - 0x1000);
+            } else {
+                val = L.read_buffer;
+                L.read_buffer = ppu_mem_rd(c, pa);
+            }
+            L.v = (L.v + ((L.ctrl & 0x04) ? 32u : 1u)) & 0xFFFF;
+            L.open_bus = val;
+            return val;
+        }
+        return 0;
+    }
+    if (a == 0x4016) {  // batch_bus.cuh:110-123
+        if (L.cstrobe) return 0x40 | (L.action & 1);
+        uint32_t bit = 1;
+        if (L.ccount < 8) {
+            bit = L.cshift & 1;
+            L.cshift >>= 1;
+            L.ccount++;
+        }
+        return 0x40 | bit;
+    }
+    if (a == 0x4017) return 0x41;
+    if (a >= 0x6000 && a < 0x8000) return c.prg_ram[a - 0x6000];
+    if (a >= 0x8000) return c.prg[a & 0x7FFF];
+    return 0;
+}
+
+// batch_bus.cuh:215-304.
+NESLE_HD void io_wr(const Ctx& c, Lane& L, uint32_t a, uint32_t val) {
+    val &= 0xFF;
+    if (a < 0x2000) { ram_wr(c, a, val); return; }
+    if (a < 0x4000) {
+        const uint32_t reg = a & 7;
+        if (reg == 0) {
+            if ((val & 0x80) && !(L.ctrl & 0x80) && (L.status & 0x80)) L.nmi = 1;
+            L.ctrl = val;
+            L.t = (L.t & 0xF3FF) | ((val & 3) << 10);
+        } else if (reg == 1) {
+            L.mask = val;
+        } else if (reg == 3) {
+            L.oam_addr = val;
+        } else if (reg == 4) {
+            c.oam[L.oam_addr & 0xFF] = (uint8_t)val;
+            L.oam_addr = (L.oam_addr + 1) & 0xFF;
+            L.flags |= kFlagOamDirty;
+        } else if (reg == 5) {
+            if (L.w == 0) {
+                L.fine_x = val & 7;
+                L.scroll_x = val;
+                L.t = (L.t & 0xFFE0) | (val >> 3);
+                L.w = 1;
+            } else {
+                L.scroll_y = val;
+                L.t = (L.t & 0x8FFF) | ((val & 7) << 12);
+                L.t = (L.t & 0xFC1F) | ((val & 0xF8) << 2);
+                L.w = 0;
+            }
+        } else if (reg == 6) {
+            if (L.w == 0) {
+                L.t = (L.t & 0x00FF) | ((val & 0x3F) << 8);
+                L.w = 1;
+            } else {
+                L.t = (L.t & 0x7F00) | val;
+                L.v = L.t;
+                L.w = 0;
+            }
+        } else if (reg == 7) {
+            ppu_mem_wr(c, L, L.v, val);
+            L.v = (L.v + ((L.ctrl & 0x04) ? 32u : 1u)) & 0xFFFF;
+        }
+        L.open_bus = val;
+        return;
+    }
+    if (a == 0x4014) { oam_dma(c, L, val); return; }
+    if (a == 0x4016) {  // batch_bus.cuh:125-133
+        const uint32_t next = val & 1;
+        if (next || L.cstrobe) { L.cshift = L.action; L.ccount = 0; }
+        L.cstrobe = next;
+        return;
+    }
+    if (a >= 0x6000 && a < 0x8000) c.prg_ram[a - 0x6000] = (uint8_t)val;
+}
+
+// Fast-path predicates: RAM and PRG reads have no side effects; writes to
+// RAM are plain stores and writes to $4000-$5FFF except $4014/$4016, and to
+// PRG, are ignored by the reference bus.
+NESLE_HD bool fast_read(uint32_t a) { return a < 0x2000 || a >= 0x8000; }
+NESLE_HD bool fast_write(uint32_t a) { return a < 0x2000; }
+
+NESLE_HD void push8(const Ctx& c, Lane& L, uint32_t v) { ram_wr(c, 0x100 | L.sp, v); L.sp = (L.sp - 1) & 0xFF; }
+NESLE_HD uint32_t pull8(const Ctx& c, Lane& L) { L.sp = (L.sp + 1) & 0xFF; return ram_rd(c, 0x100 | L.sp); }
+
+// cpu.hpp:112-123
+NESLE_HD void nmi_entry(const Ctx& c, Lane& L) {
+    push8(c, L, L.pc >> 8);
+    push8(c, L, L.pc & 0xFF);
+    push8(c, L, (L.p & ~0x10u) | 0x20u);
+    L.p |= 0x24;
+    L.pc = c.prg[0x7FFA] | (c.prg[0x7FFB] << 8);
+    L.cycles += 7;
+}
+
+// ---------------------------------------------------------------------------
+// Lazy PPU timing: batch_ppu.cuh:15-21,62-73,138-269.
+// ---------------------------------------------------------------------------
+enum : uint32_t {
+    kFrameDots = 341u * 262u,
+    kSprite0Dot = 30u * 341u + 1u,
+    kVblankDot = 241u * 341u + 1u,
+    kPreRenderDot = 261u * 341u + 1u,
+};
+
+NESLE_HD uint32_t dist_to(uint32_t cur, uint32_t ev) { return ev > cur ? ev - cur : kFrameDots - cur + ev; }
+
+NESLE_HD uint32_t next_event(const Lane& L) {  // batch_ppu.cuh:138-177
+    uint32_t n = kFrameDots - L.frame_dot;
+    uint32_t d = dist_to(L.frame_dot, kVblankDot);
+    n = d < n ? d : n;
+    d = dist_to(L.frame_dot, kPreRenderDot);
+    n = d < n ? d : n;
+    if (L.mask & 0x18) {
+        d = dist_to(L.frame_dot, kSprite0Dot);
+        n = d < n ? d : n;
+    }
+    return n;
+}
+
+
+
+// Vblank presentation snapshot (batch_ppu.cuh:223-249).  Byte arrays are
+// copied only when written since the last snapshot (the copy would otherwise
+// reproduce identical bytes).
+NESLE_HD void presentation_snapshot(const Ctx& c, Lane& L) {
+    L.ssx0 = L.lat_sx; L.ssy0 = L.lat_sy; L.sc0 = L.lat_ctrl;
+    L.ssx1 = L.scroll_x; L.ssy1 = L.scroll_y; L.sc1 = L.ctrl; L.smask = L.mask;
+    const BatchView& v = *c.view;
+    const size_t e = c.env;
+    if (L.flags & kFlagOamDirty) copy_row(v.snap_oam + e * kOamBytes, c.oam, kOamBytes);
+    if (L.flags & kFlagNtDirty) copy_row(v.snap_nt + e * kNtBytes, c.nt, kNtBytes);
+    if (L.flags & kFlagPalDirty) copy_row(v.snap_pal + e * kPalBytes, c.pal, kPalBytes);
+    L.flags &= ~(uint32_t)(kFlagOamDirty | kFlagNtDirty | kFlagPalDirty);
+}
+
+// batch_ppu.cuh:183-269; returns frames completed.
+NESLE_HD uint32_t settle(const Ctx& c, Lane& L, uint32_t dots) {
+    const uint32_t start = L.frame_dot, end = start + dots;
+    const uint32_t frames = end / kFrameDots;
+    for (uint32_t f = 0; f <= frames; ++f) {
+        const uint32_t o = f * kFrameDots;
+        if (o + kSprite0Dot > start && o + kSprite0Dot <= end && (L.mask & 0x18)) L.status |= 0x40;
+        if (o + kVblankDot > start && o + kVblankDot <= end) {
+            const bool was = (L.status & 0x80) != 0;
+            L.status |= 0x80;
+            if (!was && (L.ctrl & 0x80)) L.nmi = 1;
+            presentation_snapshot(c, L);
+        }
+        if (o + kPreRenderDot > start && o + kPreRenderDot <= end) {
+            L.status &= 0x1F;  // vblank, sprite-0 and overflow cleared
+            L.nmi = 0;
+            L.lat_sx = L.scroll_x; L.lat_sy = L.scroll_y; L.lat_ctrl = L.ctrl;
+        }
+    }
+    L.frame_dot = end % kFrameDots;
+    L.frame += frames;
+    return frames;
+}
+
+// ---------------------------------------------------------------------------
+// Side path: instructions with several stack/bus transfers (cpu.hpp:586,
+// 666-694): JMP (ind), JSR, RTS, RTI, BRK.  `b1`,`b2` are the operand bytes.
+// ---------------------------------------------------------------------------
+NESLE_HD void exec_special(const Ctx& c, Lane& L, uint32_t op, uint32_t b1, uint32_t b2) {
+    const uint32_t b16 = b1 | (b2 << 8);
+    switch (op) {
+        case 0x6C: {  // JMP (ind) with the page-wrap fetch bug
+            const uint32_t lo = io_rd(c, L, b16);
+            const uint32_t hi = io_rd(c, L, (b16 & 0xFF00) | ((b16 + 1) & 0xFF));
+            L.pc = lo | (hi << 8);
+            break;
+        }
+        case 0x20: {  // JSR
+            const uint32_t ret = (L.pc + 2) & 0xFFFF;
+            push8(c, L, ret >> 8);
+            push8(c, L, ret & 0xFF);
+            L.pc = b16;
+            break;
+        }
+        case 0x60: {  // RTS
+            const uint32_t lo = pull8(c, L), hi = pull8(c, L);
+            L.pc = ((lo | (hi << 8)) + 1) & 0xFFFF;
+            break;
+        }
+        case 0x40: {  // RTI
+            L.p = (pull8(c, L) | 0x20) & ~0x10u;
+            const uint32_t lo = pull8(c, L), hi = pull8(c, L);
+            L.pc = lo | (hi << 8);
+            break;
+        }
+        default: {  // BRK
+            const uint32_t ret = (L.pc + 2) & 0xFFFF;
+            push8(c, L, ret >> 8);
+            push8(c, L, ret & 0xFF);
+            push8(c, L, L.p | 0x30);
+            L.p |= 0x24;
+            L.pc = io_rd(c, L, 0xFFFE) | (io_rd(c, L, 0xFFFF) << 8);
+            break;
+        }
+    }
+}
+
+#if defined(__CUDA_ARCH__)
+#define NESLE_FUNNEL(lo, hi, s) __funnelshift_r((lo), (hi), (s))
+#else
+#define NESLE_FUNNEL(lo, hi, s) ((uint32_t)((((uint64_t)(hi) << 32) | (lo)) >> ((s) & 31)))
+#endif
+
+// ---------------------------------------------------------------------------
+// One instruction on the uniform datapath: cpu.hpp:378-730 restated as data
+// flow.  Returns the opcode, or -1 when the env froze (status word set).
+// ---------------------------------------------------------------------------
+NESLE_HD int exec_instruction(const Ctx& c, Lane& L) {
+    const uint32_t pc = L.pc;
+    uint32_t op, b1, b2;
+    if (pc - 0x8000u <= 0x7FFDu) {
+        const uint32_t wi = (pc & 0x7FFF) >> 2;
+        const uint32_t* p32 = reinterpret_cast<const uint32_t*>(c.prg);
+        const uint32_t bytes = NESLE_FUNNEL(p32[wi], p32[wi + 1], (pc & 3) * 8);
+        op = bytes & 0xFF;
+        b1 = (bytes >> 8) & 0xFF;
+        b2 = (bytes >> 16) & 0xFF;
+    } else {
+        // Outside the shared PRG window (code in RAM, PRG-RAM or I/O space, or
+        // an instruction running past $FFFF): fetch the bytes this opcode
+        // uses through the full bus, in order, as cpu.hpp:382-392 does.
+        op = io_rd(c, L, pc);
+        const uint64_t dd = c.dec[op];
+        const uint32_t len = (dd & (1ull << D_ILLEGAL)) ? 0u : dfield(dd, D_LEN, 2);
+        b1 = len >= 1 ? io_rd(c, L, (pc + 1) & 0xFFFF) : 0u;
+        b2 = len >= 2 ? io_rd(c, L, (pc + 2) & 0xFFFF) : 0u;
+    }
+    const uint64_t d = c.dec[op];
+    if (d & (1ull << D_ILLEGAL)) {
+        L.status_word = NESLE_STATUS_ILLEGAL | (op << 16) | pc;
+        return -1;
+    }
+    const uint32_t len = dfield(d, D_LEN, 2) + 1;
+    uint32_t cyc = dfield(d, D_CYC, 3);
+    if (d & (1ull << D_SPECIAL)) {
+        exec_special(c, L, op, b1, b2);
+        L.cycles += cyc;
+        return (int)op;
+    }
+
+    // ---- effective address ----
+    const uint32_t idx_sel = dfield(d, D_IDX, 2);
+    const uint32_t idx = idx_sel == 1 ? L.x : (idx_sel == 2 ? L.y : 0u);
+    const uint32_t base_sel = dfield(d, D_BASE, 2);
+    uint32_t base = base_sel == 0 ? b1 : (b1 | (b2 << 8));
+    if (base_sel == 2) {  // (zp,X) / (zp),Y pointer from zero page
+        const uint32_t ptr = (b1 + ((d >> D_INDX) & 1 ? L.x : 0u)) & 0xFF;
+        base = ram_rd(c, ptr) | (ram_rd(c, (ptr + 1) & 0xFF) << 8);
+    }
+    uint32_t addr = (base + idx) & 0xFFFF;
+    if ((d >> D_ZPW) & 1) addr &= 0xFF;
+    if ((d >> D_PAGE) & 1) cyc += ((base ^ addr) & 0xFF00) ? 1u : 0u;
+    if (base_sel == 3) addr = 0x100 | ((L.sp + ((d >> D_PULL) & 1)) & 0xFF);
+
+    // ---- operand read ----
+    uint32_t m = b1;  // immediate
+    if ((d >> D_RD) & 1) {
+        if (fast_read(addr)) {
+            m = addr < 0x2000 ? c.ram[ram_off(c, addr)] : c.prg[addr & 0x7FFF];
+        } else {
+            m = io_rd(c, L, addr);
+        }
+    }
+
+    // ---- ALU ----
+    const uint32_t opa_sel = dfield(d, D_OPA, 3);
+    uint32_t opa;
+    switch (opa_sel) {
+        case A_A: opa = L.a; break;
+        case A_X: opa = L.x; break;
+        case A_Y: opa = L.y; break;
+        case A_SP: opa = L.sp; break;
+        case A_M: opa = m; break;
+        case A_PHP: opa = L.p | 0x30; break;
+        default: opa = 0; break;
+    }
+    const uint32_t carry_in = ((d >> D_CINC) & 1) ? (L.p & 1) : ((d >> D_CIN1) & 1);
+    const uint32_t opb = (((d >> D_BM) & 1) ? m : 0u) ^ (((d >> D_BX) & 1) ? 0xFFu : 0u);
+    const uint32_t sum = opa + opb + carry_in;
+    const uint32_t unit = dfield(d, D_UNIT, 3);
+    const uint32_t rot_c = ((d >> D_ROT) & 1) ? (L.p & 1) : 0u;
+    uint32_t r, cout;
+    switch (unit) {
+        case U_AND: r = opa & m; cout = 0; break;
+        case U_OR: r = opa | m; cout = 0; break;
+        case U_XOR: r = opa ^ m; cout = 0; break;
+        case U_SHL: r = ((opa << 1) | rot_c) & 0xFF; cout = opa >> 7; break;
+        case U_SHR: r = (opa >> 1) | (rot_c << 7); cout = opa & 1; break;
+        default: r = sum & 0xFF; cout = (sum >> 8) & 1; break;
+    }
+
+    // ---- flags ----
+    const uint32_t flg = dfield(d, D_FLG, 2);
+    uint32_t p = L.p;
+    if (flg) {
+        uint32_t mask = 0x82, val = (r & 0x80) | (r == 0 ? 0x02u : 0u);
+        if (flg >= F_NZC) { mask |= 0x01; val |= cout; }
+        if (flg == F_NZCV) { mask |= 0x40; val |= ((~(opa ^ opb) & (opa ^ r)) & 0x80) ? 0x40u : 0u; }
+        p = (p & ~mask) | val;
+    }
+    if ((d >> D_BIT) & 1) p = (p & ~0xC2u) | (m & 0xC0) | (r == 0 ? 0x02u : 0u);
+    const uint32_t fcm = dfield(d, D_FCM, 8);
+    p = (p & ~fcm) | (((d >> D_FCV) & 1) ? fcm : 0u);
+    if ((d >> D_WP) & 1) p = (r | 0x20) & ~0x10u;
+    // The reference forces the unused bit only when an instruction writes a
+    // flag (set_flag, cpu.hpp:52-59); stores, branches and jumps leave P as is.
+    if (flg | ((d >> D_BIT) & 1) | fcm) p |= 0x20;
+
+    // ---- memory write ----
+    if ((d >> D_WM) & 1) {
+        if (fast_write(addr)) c.ram[ram_off(c, addr)] = (uint8_t)r;
+        else io_wr(c, L, addr, r);
+    }
+
+    // ---- register write-back ----
+    if ((d >> D_WA) & 1) L.a = r;
+    if ((d >> D_WX) & 1) L.x = r;
+    if ((d >> D_WY) & 1) L.y = r;
+    if ((d >> D_WSP) & 1) L.sp = r;
+    const uint32_t spd = dfield(d, D_SPD, 2);
+    if (spd) L.sp = (L.sp + (spd == 1 ? 0xFFu : 1u)) & 0xFF;
+
+    // ---- next PC ----
+    uint32_t npc = pc + len;
+    if ((d >> D_BR) & 1) {
+        const uint32_t flag = (L.p >> dfield(d, D_BRF, 3)) & 1;  // flags before this instruction
+        if (flag == ((d >> D_BRP) & 1)) {
+            const uint32_t target = (npc + (uint32_t)(int32_t)(int8_t)b1) & 0xFFFF;
+            cyc += 1 + (((npc ^ target) & 0xFF00) ? 1u : 0u);
+            npc = target;
+        }
+    }
+    if ((d >> D_JMP) & 1) npc = b1 | (b2 << 8);
+    L.p = p;
+    L.pc = npc & 0xFFFF;
+    L.cycles += cyc;
+    return (int)op;
+}
+
+// ---------------------------------------------------------------------------
+// Per-launch loop: kernels.cu:19-104 as a per-lane state machine so a warp can
+// keep executing instructions for lanes whose frames end at different times.
+// ---------------------------------------------------------------------------
+NESLE_HD void frame_end(const Ctx& c, Lane& L) {
+    if (L.pending) {
+        L.fcomp += settle(c, L, L.pending);
+        L.pending = 0;
+        L.horizon = next_event(L);
+    }
+    L.tot_instr += L.instr;
+    L.tot_frames += L.fcomp;
+    if (L.fcomp == 0 && L.instr >= c.max_instr) L.budget++;
+    L.fidx++;
+    if (L.status_word) L.fidx = c.frameskip;  // frozen env: no further frames
+    L.instr = 0;
+    L.fcomp = 0;
+}
+
+// Loop-top bookkeeping (kernels.cu:46-56).  Returns false when the lane has
+// finished all frames of this step.
+NESLE_HD bool loop_top(const Ctx& c, Lane& L) {
+    for (;;) {
+        if (L.fidx >= c.frameskip) return false;
+        if (L.status_word || L.instr >= c.max_instr || L.fcomp != 0) {
+            frame_end(c, L);
+            continue;
+        }
+        if (L.pending >= L.horizon) {
+            L.fcomp += settle(c, L, L.pending);
+            L.pending = 0;
+            L.horizon = next_event(L);
+            if (L.fcomp) { frame_end(c, L); continue; }
+        }
+        return true;
+    }
+}
+
+// One loop iteration after loop_top() returned true:
+// step_batch_console_instruction_lazy (batch_console.hpp:77-109) plus the idle
+// fast-forward (kernels.cu:66-76, batch_console.hpp:129-152).
+NESLE_HD void step_once(const Ctx& c, Lane& L) {
+    const uint64_t before = L.cycles;
+    if (L.nmi) {
+        L.nmi = 0;
+        nmi_entry(c, L);
+    }
+    const uint32_t op_pc = L.pc;
+    const int op = exec_instruction(c, L);
+    if (op < 0) return;  // frozen: loop_top ends the frame
+    if (L.dma) {
+        L.cycles += L.dma;
+        L.dma = 0;
+    }
+    L.pending += (uint32_t)(L.cycles - before) * 3u;
+    L.instr++;
+    if (op == 0x4C && L.pc == op_pc && L.fcomp == 0) {
+        L.fcomp += settle(c, L, L.pending);
+        L.pending = 0;
+        const uint32_t jumps = (next_event(L) + 8u) / 9u;
+        if (jumps) {
+            L.cycles += (uint64_t)jumps * 3u;
+            L.fcomp += settle(c, L, jumps * 9u);
+        }
+        L.horizon = next_event(L);
+    }
+}
+
+NESLE_HD void begin_step(Lane& L) {
+    L.pending = 0;
+    L.horizon = next_event(L);
+    L.instr = 0;
+    L.fcomp = 0;
+    L.fidx = 0;
+    L.tot_instr = 0;
+    L.tot_frames = 0;
+    L.budget = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Reward and done: batch_step.cuh:41-106 plus the configuration predicates.
+// ---------------------------------------------------------------------------
+NESLE_HD void reward_done(const Ctx& c, Lane& L, float& reward, uint8_t& done) {
+    const BatchView& v = *c.view;
+    const int x = (int)ram_rd(c, 0x6D) * 0x100 + (int)ram_rd(c, 0x86);
+    const int time = (int)(ram_rd(c, 0x7F8) & 0xF) * 100 + (int)(ram_rd(c, 0x7F9) & 0xF) * 10 +
+                     (int)(ram_rd(c, 0x7FA) & 0xF);
+    const uint32_t ps = ram_rd(c, 0x0E);
+    const bool dying = ps == 0x0B || ram_rd(c, 0xB5) > 1;
+    const bool dead = ps == 0x06;
+    const bool over = ram_rd(c, 0x75A) == 0xFF;
+    bool stage_over = false;
+    const uint32_t fl = ram_rd(c, 0x1D);
+    for (uint32_t i = 0; i < 5; ++i) {
+        const uint32_t e = ram_rd(c, 0x16 + i);
+        stage_over |= (e == 0x2D || e == 0x31) && fl == 3;
+    }
+    const bool flag = ram_rd(c, 0x770) == 2 || stage_over;
+    int rx = x - L.prev_x;
+    if (rx < -5 || rx > 5) rx = 0;
+    int rt = time - L.prev_time;
+    if (rt > 0) rt = 0;
+    reward = (float)(rx + rt + ((dying || dead) ? -25 : 0));
+    bool dn = flag || dying || dead || over;
+    if (v.done_mode == kDoneRamEq) dn = ram_rd(c, v.done_a & 0x7FF) == (v.done_b & 0xFF);
+    else if (v.done_mode == kDoneFrameLimit) dn = L.frame >= frame_limit(v, c.env, L.episode);
+    done = dn ? 1 : 0;
+    L.prev_x = x;
+    L.prev_time = time;
+}
+
+// ---------------------------------------------------------------------------
+// Resets on global memory: batch_step.cuh:109-242.
+// ---------------------------------------------------------------------------
+NESLE_HD void cold_reset(const BatchView& v, uint32_t env, EnvRecord& r) {
+    const uint32_t episode = r.episode;
+    memset(&r, 0, sizeof(r));
+    r.episode = episode;
+    r.pc = v.reset_vector;
+    r.sp = 0xFD;
+    r.p = 0x24;
+    r.cycles = 7;
+    r.ctrl_count = 8;
+    r.flags = kFlagNtDirty | kFlagPalDirty | kFlagOamDirty;
+    const size_t e = env;
+    zero_row(v.ram + e * kRamBytes, kRamBytes);
+    zero_row(v.prg_ram + e * kPrgRamBytes, kPrgRamBytes);
+    zero_row(v.nt + e * kNtBytes, kNtBytes);
+    zero_row(v.pal + e * kPalBytes, kPalBytes);
+    zero_row(v.oam + e * kOamBytes, kOamBytes);
+}
+
+NESLE_HD void warm_reset(const BatchView& v, uint32_t env, EnvRecord& r) {
+    const uint32_t lvl = v.env_to_level[env];
+    const BankRecord& s = v.bank[lvl];
+    const uint32_t episode = r.episode;
+    memset(&r, 0, sizeof(r));
+    r.episode = episode;
+    r.pc = s.pc; r.a = s.a; r.x = s.x; r.y = s.y; r.sp = s.sp; r.p = s.p; r.cycles = s.cycles;
+    r.ctrl_count = 8;
+    r.ppu_ctrl = s.ctrl; r.ppu_mask = s.mask; r.ppu_status = s.status; r.oam_addr = s.oam_addr;
+    r.v = s.v; r.t = s.t; r.fine_x = s.fine_x; r.w = s.w; r.open_bus = s.open_bus; r.read_buffer = s.read_buffer;
+    r.prev_x = s.prev_x; r.prev_time = s.prev_time;
+    r.flags = kFlagNtDirty | kFlagPalDirty | kFlagOamDirty;
+    const size_t e = env;
+    copy_row(v.ram + e * kRamBytes, v.bank_ram + (size_t)lvl * kRamBytes, kRamBytes);
+    copy_row(v.prg_ram + e * kPrgRamBytes, v.bank_prg_ram + (size_t)lvl * kPrgRamBytes, kPrgRamBytes);
+    copy_row(v.nt + e * kNtBytes, v.bank_nt + (size_t)lvl * kNtBytes, kNtBytes);
+    copy_row(v.pal + e * kPalBytes, v.bank_pal + (size_t)lvl * kPalBytes, kPalBytes);
+    copy_row(v.oam + e * kOamBytes, v.bank_oam + (size_t)lvl * kOamBytes, kOamBytes);
+}
+
+// The reset kernels of the reference rewrite the console state only: the
+// presentation-snapshot scalars and the per-step statistics of the step that
+// triggered the reset survive.
+NESLE_HD void reset_env(const BatchView& v, uint32_t env, EnvRecord& r) {
+    const EnvRecord keep = r;
+    if (v.num_levels) warm_reset(v, env, r);
+    else cold_reset(v, env, r);
+    r.lat_sx = keep.lat_sx; r.lat_sy = keep.lat_sy; r.lat_ctrl = keep.lat_ctrl;
+    r.snap_sx_start = keep.snap_sx_start; r.snap_sy_start = keep.snap_sy_start;
+    r.snap_ctrl_start = keep.snap_ctrl_start; r.snap_sx_end = keep.snap_sx_end;
+    r.snap_sy_end = keep.snap_sy_end; r.snap_ctrl_end = keep.snap_ctrl_end; r.snap_mask = keep.snap_mask;
+    r.stat_instructions = keep.stat_instructions;
+    r.stat_frames = keep.stat_frames;
+    r.stat_budget_hits = keep.stat_budget_hits;
+}
+
+// cuda_module.cu:1443-1463: presentation snapshot from live state.
+NESLE_HD void seed_presentation(const BatchView& v, uint32_t env, EnvRecord& r) {
+    const size_t e = env;
+    copy_row(v.snap_nt + e * kNtBytes, v.nt + e * kNtBytes, kNtBytes);
+    copy_row(v.snap_pal + e * kPalBytes, v.pal + e * kPalBytes, kPalBytes);
+    copy_row(v.snap_oam + e * kOamBytes, v.oam + e * kOamBytes, kOamBytes);
+    r.snap_mask = r.ppu_mask;
+    r.lat_sx = r.snap_sx_start = r.snap_sx_end = r.scroll_x;
+    r.lat_sy = r.snap_sy_start = r.snap_sy_end = r.scroll_y;
+    r.lat_ctrl = r.snap_ctrl_start = r.snap_ctrl_end = r.ppu_ctrl;
+    r.flags &= ~(uint8_t)(kFlagNtDirty | kFlagPalDirty | kFlagOamDirty);
+}
+
+// ---------------------------------------------------------------------------
+// Whole-step helpers shared by the CUDA kernel and the host unit-test build.
+// ---------------------------------------------------------------------------
+
+// Runs env `c.env` for one env-step (frameskip frames).  Its RAM must be
+// staged at `c.ram`; `rec` is updated in place.
+NESLE_HD void run_env_step(const Ctx& c, EnvRecord& rec, uint8_t action, float& reward, uint8_t& done) {
+    Lane L;
+    load_lane(L, rec, action);
+    begin_step(L);
+    while (loop_top(c, L)) step_once(c, L);
+    reward_done(c, L, reward, done);
+    store_lane(L, rec);
+}
+
+// Outputs and the fused auto-reset of step_device (cuda_module.cu:635-656):
+// last_* hold the pre-reset values; the reset clears rewards/done.
+// The env's RAM must already be back in global memory.  Returns true when
+// the env's status word became non-zero during this step.
+NESLE_HD bool finish_env(const BatchView& v, uint32_t env, EnvRecord& rec, uint32_t status_before,
+                         float reward, uint8_t done, bool device_api, bool auto_reset) {
+    v.rewards[env] = reward;
+    v.done[env] = done;
+    const bool faulted = rec.status != 0 && status_before == 0;
+    if (device_api) {
+        v.last_rewards[env] = reward;
+        v.last_done[env] = done;
+        if (auto_reset && done) {
+            rec.episode++;
+            reset_env(v, env, rec);
+            v.rewards[env] = 0.0f;
+            v.done[env] = 0;
+        }
+    }
+    return faulted;
+}
+
+}  // namespace nesle

@@ -1,0 +1,191 @@
+"""GPU parity: libnesle_b200.so through its C ABI against the CPU checker.
+
+Bit-exact per-env RAM, CPU registers, cycles, PPU state, done/reward and
+palette-index frames after every step, on every benchmark configuration at
+sizes the checker runs in seconds, plus size-independent properties at the
+full 65,536-env configuration.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import kat_roms as kat
+from harness import STATE_FIELDS, GpuCore, assert_same, run_lockstep
+from nesle_b200 import workloads as w
+from oracle import Oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from nesle_b200 import build
+    build.build()
+
+
+@pytest.mark.parametrize("make,auto_reset,n", [(w.config1, False, 64), (w.config2, True, 200),
+                                               (w.config4, True, 200)])
+def test_configs_lockstep(make, auto_reset, n):
+    """Every step, every field, against the checker (200 envs = 2 full CTAs + a partial one)."""
+    run_lockstep(make, n, 6, auto_reset, [GpuCore])
+
+
+def test_config1_full_length():
+    """Config 1 as specified: 64 envs, 600 frames (150 env-steps), from power-on."""
+    run_lockstep(w.config1, 64, 150, False, [GpuCore], check_every=10)
+
+
+def test_frame_limit_auto_reset_many_episodes():
+    def short():
+        wl = w.config4()
+        wl.done_args = (5, 17)
+        return wl
+    _, _, dones = run_lockstep(short, 97, 24, True, [GpuCore])
+    assert dones > 50
+
+
+@pytest.mark.parametrize("rom,snaps", [
+    (kat.LDA_TAX_INX_STA, []), (kat.JSR_RTS, []), (kat.BNE_PAGE_CROSS, []), (kat.SEC_SBC, []),
+    (kat.NMI_ROM, []), (kat.DMA_ROM, [kat.dma_snapshot()]), (kat.IDLE_ROM, [])])
+def test_known_answer_roms(rom, snaps):
+    o = Oracle(3, 2, rom, snaps)
+    g = GpuCore(3, 2, rom, snaps)
+    for _ in range(3):
+        a = np.array([0x81, 0x00, 0xFF], np.uint8)
+        o.step(a, auto_reset=False)
+        g.step(a, auto_reset=False)
+        assert_same(o, g)
+
+
+@pytest.mark.parametrize("case", kat.REWARD_CASES)
+def test_reward_known_answers(case):
+    (pp, ps, pt), (cp, cs, ct, state), reward, done = case
+    g = GpuCore(1, 1, kat.IDLE_ROM, [kat.mario_snapshot(pp, ps, pt)])
+    for addr, val in ((0x6D, cp), (0x86, cs), (0x0E, state), (0x7F8, ct // 100), (0x7F9, (ct // 10) % 10),
+                      (0x7FA, ct % 10)):
+        g.poke_ram(addr, val)
+    g.step(np.zeros(1, np.uint8), auto_reset=False)
+    assert g.get("last_reward")[0] == reward and g.get("last_done")[0] == done
+
+
+def test_every_official_opcode():
+    from test_core_host import _single_instruction_cases
+
+    for opc, rom, snap in _single_instruction_cases(3, 1):
+        o = Oracle(1, 1, rom, [snap])
+        g = GpuCore(1, 1, rom, [snap])
+        o.step(np.zeros(1, np.uint8), auto_reset=False)
+        g.step(np.zeros(1, np.uint8), auto_reset=False)
+        try:
+            assert_same(o, g, ("pc", "a", "x", "y", "sp", "p", "cycles", "ram", "prg_ram", "status"))
+        except AssertionError as e:
+            raise AssertionError(f"opcode {opc:#04x}: {e}") from None
+
+
+def test_render_index_rgb_gray_match_checker():
+    from test_core_host import render_snapshots
+
+    wl = w.config4()
+    n = 8
+    snaps = render_snapshots(11, 4, wl.rom.loop_head)
+    kw = dict(env_to_level=np.arange(n) % 4, done_mode=wl.done_mode, done_args=wl.done_args, seed=wl.seed)
+    o = Oracle(n, 4, wl.rom.image, snaps, **kw)
+    g = GpuCore(n, 4, wl.rom.image, snaps, **kw)
+    for s in range(3):
+        a = wl.actions(np.arange(n), s)
+        o.step(a)
+        g.step(a)
+    ro, rg = o.render(), g.render()
+    for k in ("index", "rgb", "gray84"):
+        np.testing.assert_array_equal(ro[k], rg[k], err_msg=k)
+    assert len(np.unique(ro["index"])) > 8
+
+
+def test_reset_envs_poke_and_host_step():
+    wl = w.config4()
+    n = 100
+    kw = dict(env_to_level=wl.env_to_level(np.arange(n)), done_mode=wl.done_mode, done_args=wl.done_args,
+              seed=wl.seed)
+    o = Oracle(n, 4, wl.rom.image, wl.snapshots, **kw)
+    g = GpuCore(n, 4, wl.rom.image, wl.snapshots, **kw)
+    a = wl.actions(np.arange(n), 0)
+    o.step(a, device_api=False)
+    g.step(a, device_api=False)
+    assert_same(o, g)
+    mask = (np.arange(n) % 3 == 0).astype(np.uint8)
+    o.reset_envs(mask)
+    g.reset_envs(mask)
+    o.poke_ram(0x7F0, 0x99)
+    g.poke_ram(0x7F0, 0x99)
+    assert_same(o, g)
+    for s in range(1, 3):
+        a = wl.actions(np.arange(n), s)
+        o.step(a)
+        g.step(a)
+        assert_same(o, g)
+    o.reset()
+    g.reset()
+    assert_same(o, g)
+
+
+def test_illegal_opcode_sets_status_without_fault():
+    rom = kat.rom_with({0x8000: bytes([0xA9, 0x05, 0x02])})
+    o = Oracle(4, 2, rom)
+    g = GpuCore(4, 2, rom)
+    for _ in range(2):
+        o.step(np.zeros(4, np.uint8), auto_reset=False)
+        g.step(np.zeros(4, np.uint8), auto_reset=False)
+        assert_same(o, g)
+    assert (g.get("status") == (0x80000000 | 0x020000 | 0x8002)).all()
+
+
+@pytest.mark.parametrize("offset", [0, 32768 - 48, 65536 - 96])
+def test_full_size_config4_windows_match_checker(offset):
+    """65,536 envs on the GPU; three windows of 96 envs re-run on the checker."""
+    full = _full_size_run(steps=3)
+    wl = w.config4()
+    n = 96
+    env = np.arange(offset, offset + n)
+    o = Oracle(n, 4, wl.rom.image, wl.snapshots, env_to_level=wl.env_to_level(env), done_mode=wl.done_mode,
+               done_args=wl.done_args, seed=wl.seed, env_offset=offset)
+    for s in range(3):
+        o.step(wl.actions(env, s))
+    for f in ("pc", "a", "x", "y", "sp", "p", "cycles", "ram", "oam", "frame", "last_reward", "last_done"):
+        np.testing.assert_array_equal(o.get(f), full[f][offset:offset + n], err_msg=f)
+
+
+_FULL_CACHE: dict = {}
+
+
+def _full_size_run(steps: int) -> dict:
+    if steps not in _FULL_CACHE:
+        wl = w.config4()
+        n = 65536
+        env = np.arange(n)
+        g = GpuCore(n, 4, wl.rom.image, wl.snapshots, env_to_level=wl.env_to_level(env), done_mode=wl.done_mode,
+                    done_args=wl.done_args, seed=wl.seed)
+        for s in range(steps):
+            g.step(wl.actions(env, s))
+        _FULL_CACHE[steps] = {f: g.get(f) for f in ("pc", "a", "x", "y", "sp", "p", "cycles", "ram", "oam", "frame",
+                                                    "last_reward", "last_done", "status")}
+        del g
+    return _FULL_CACHE[steps]
+
+
+def test_full_size_properties():
+    """Size-independent checks at full size: healthy, deterministic, envs diverged."""
+    a = _full_size_run(steps=3)
+    assert (a["status"] == 0).all()
+    assert (a["frame"] == 12).all()  # 3 env-steps x frameskip 4
+    assert len(np.unique(a["pc"])) > 100  # joypad-driven divergence
+    wl = w.config4()
+    g = GpuCore(65536, 4, wl.rom.image, wl.snapshots, env_to_level=wl.env_to_level(np.arange(65536)),
+                done_mode=wl.done_mode, done_args=wl.done_args, seed=wl.seed)
+    for s in range(3):
+        g.step(wl.actions(np.arange(65536), s))
+    np.testing.assert_array_equal(g.get("ram"), a["ram"])
+    np.testing.assert_array_equal(g.get("cycles"), a["cycles"])
