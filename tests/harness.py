@@ -152,34 +152,18 @@ class GpuCore(_Common):
                                        int(auto_reset), None))
 
     def render(self) -> dict:
-        n = self.num_envs
-        shapes = {_lib.RENDER_RGB: ("rgb", (n, 240, 256, 3), _lib.PTR_FRAMES_RGB),
-                  _lib.RENDER_INDEX: ("index", (n, 240, 256), _lib.PTR_FRAMES_INDEX),
-                  _lib.RENDER_GRAY84: ("gray84", (n, 84, 84), _lib.PTR_OBS_GRAY84)}
         out = {}
-        for mode, (key, shape, which) in shapes.items():
+        for mode, key, field in ((_lib.RENDER_RGB, "rgb", "frames_rgb"), (_lib.RENDER_INDEX, "index", "frames_index"),
+                                 (_lib.RENDER_GRAY84, "gray84", "obs_gray84")):
             _lib.check(self.lib.nesle_render(self._h, mode, None))
-            _lib.check(self.lib.nesle_sync(self._h))
-            ptr, nbytes = ctypes.c_void_p(), ctypes.c_uint64()
-            _lib.check(self.lib.nesle_device_ptr(self._h, which, ctypes.byref(ptr), ctypes.byref(nbytes)))
-            host = np.zeros(shape, np.uint8)
-            assert nbytes.value == host.nbytes
-            _copy_device_to_host(ptr.value, host)
+            dtype, shape = _lib.FIELDS[field]
+            host = np.zeros((self.num_envs, *shape), dtype)
+            self._copy(field, host)
             out[key] = host
         return out
 
     def _copy(self, name, out):
         _lib.check(self.lib.nesle_copy_field(self._h, name.encode(), out.ctypes.data, out.nbytes))
-
-
-def _copy_device_to_host(ptr: int, host: np.ndarray) -> None:
-    import torch
-
-    class _Cai:
-        __cuda_array_interface__ = {"shape": (host.nbytes,), "typestr": "|u1", "data": (ptr, True), "version": 3}
-
-    t = torch.as_tensor(_Cai(), device="cuda")
-    host.reshape(-1)[:] = t.cpu().numpy()
 
 
 def assert_same(ref, other, fields=STATE_FIELDS, label: str = "") -> None:
