@@ -2,6 +2,7 @@
 // snapshot bank upload and kernel launches for one batch.
 #include <cuda_runtime.h>
 #include <stddef.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <string>
@@ -59,6 +60,8 @@ struct nesle_batch {
     uint8_t* d_frames_index = nullptr;
     uint8_t* d_gray84 = nullptr;
     cudaEvent_t done_event = nullptr;
+    uint32_t step_variant = kStepGlobalRam;
+    uint32_t step_threads = 0;
 
     template <class T>
     int alloc(T** out, size_t count, const char* label) {
@@ -239,6 +242,15 @@ static int create_impl(const nesle_create_args* a, nesle_batch* b) {
     v.actions = nullptr;
     TRY(b->alloc(&b->dv, 1, "batch view"));
     CUDA_TRY(cudaMemcpy(b->dv, &v, sizeof(BatchView), cudaMemcpyHostToDevice), "batch view upload");
+    // Step-kernel placement of env RAM (default: in place in global memory);
+    // NESLE_STEP_KERNEL=shared stages it in shared memory, 96 envs per SM.
+    if (const char* sv = getenv("NESLE_STEP_KERNEL")) {
+        if (strcmp(sv, "global") == 0) b->step_variant = kStepGlobalRam;
+        else if (strcmp(sv, "shared") == 0) b->step_variant = kStepSharedRam;
+    }
+    int sms = 0;
+    CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, a->device), "SM count");
+    b->step_threads = global_step_threads(b->n, static_cast<uint32_t>(sms));
     CUDA_TRY(cudaEventCreateWithFlags(&b->done_event, cudaEventDisableTiming), "create event");
     CUDA_TRY(launch_reset(b->dv, b->n, nullptr, true, nullptr), "initial reset");
     CUDA_TRY(cudaEventRecord(b->done_event, nullptr), "record event");
@@ -317,7 +329,7 @@ int nesle_step(nesle_batch* b, const void* actions, int dtype, int on_device, in
         a8 = b->d_host_actions;
     }
     uint32_t flags = (device_api ? kStepDeviceApi : 0u) | (auto_reset ? kStepAutoReset : 0u);
-    return finish(b, s, launch_step(b->dv, b->n, a8, a64, flags, s), "step kernel");
+    return finish(b, s, launch_step(b->dv, b->n, a8, a64, flags, b->step_variant, b->step_threads, s), "step kernel");
 }
 
 static int ensure_frames(nesle_batch* b, int which) {
@@ -454,8 +466,8 @@ int nesle_get_info(nesle_batch* b, nesle_info* out) {
     out->frameskip = b->frameskip;
     out->num_levels = b->num_levels;
     out->device = static_cast<uint32_t>(b->device);
-    out->envs_per_block = kStepSlots;
-    out->smem_bytes_per_block = static_cast<uint32_t>(step_smem_bytes());
+    out->envs_per_block = b->step_variant == kStepGlobalRam ? b->step_threads : kStepSlots;
+    out->smem_bytes_per_block = b->step_variant == kStepGlobalRam ? 32768 + 16 + 256 * 32 : static_cast<uint32_t>(step_smem_bytes());
     return NESLE_OK;
 }
 

@@ -1,6 +1,7 @@
 // kernels.cu -- sm_100a kernels of the batched NES core.
 //
-//   step_kernel     one env-step of 96 envs per CTA (env state in shared memory)
+//   step_kernel_global  one env-step per thread, env RAM in place (default)
+//   step_kernel     one env-step per thread, env RAM staged in shared memory
 //   reset_kernel    masked or full snapshot/cold reset
 //   poke_kernel     one RAM byte in every env
 //   render_kernel   colour index or RGB per pixel from the presentation snapshot
@@ -13,15 +14,17 @@
 
 namespace nesle {
 
-__constant__ DecodeTable kDecodeConst = dt::build();
+__constant__ EntryTable kEntriesConst = dt::build_entries();
 __constant__ uint8_t kPaletteRgb[192] = NESLE_PALETTE_RGB;
 
 // --------------------------------------------------------------------------
-// Env step.  One CTA = kStepSlots envs = kStepSlots threads (3 warps) and one
-// CTA per SM: 32 KB PRG + 2 KB decode table + 96 x 2 KB interleaved RAM.
+// Env step with RAM staged in shared memory.  One CTA = kStepSlots envs =
+// kStepSlots threads: 32 KB PRG + 8 KB execution entries + kStepSlots x 2 KB
+// interleaved RAM.  Kept as the alternative placement (NESLE_STEP_KERNEL=shared);
+// the in-place kernel below is the default.
 // --------------------------------------------------------------------------
 constexpr uint32_t kPrgSmem = 32768 + 16;  // +16: the two-word fetch at $FFFC-$FFFD reads one word past the ROM
-constexpr uint32_t kDecSmem = 256 * 8;
+constexpr uint32_t kDecSmem = 256 * sizeof(Entry);
 
 __device__ __forceinline__ uint32_t* ram_word(uint8_t* slot, uint32_t word) {
     return reinterpret_cast<uint32_t*>(slot + word * 4u * kStepSlots);
@@ -32,7 +35,7 @@ step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
             const long long* __restrict__ act64, uint32_t flags) {
     extern __shared__ __align__(16) uint8_t smem[];
     uint8_t* s_prg = smem;
-    uint64_t* s_dec = reinterpret_cast<uint64_t*>(smem + kPrgSmem);
+    Entry* s_dec = reinterpret_cast<Entry*>(smem + kPrgSmem);
     uint8_t* s_ram = smem + kPrgSmem + kDecSmem;
     const BatchView& v = *vp;
     const uint32_t tid = threadIdx.x;
@@ -40,7 +43,8 @@ step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
     const uint4* prg_src = reinterpret_cast<const uint4*>(v.prg);
     for (uint32_t i = tid; i < 2048; i += blockDim.x) reinterpret_cast<uint4*>(s_prg)[i] = prg_src[i];
     if (tid == 0) reinterpret_cast<uint4*>(s_prg)[2048] = make_uint4(0, 0, 0, 0);
-    for (uint32_t i = tid; i < 256; i += blockDim.x) s_dec[i] = kDecodeConst.e[i];
+    const uint4* ent_src = reinterpret_cast<const uint4*>(&kEntriesConst);
+    for (uint32_t i = tid; i < kDecSmem / 16; i += blockDim.x) reinterpret_cast<uint4*>(s_dec)[i] = ent_src[i];
 
     const uint32_t env = blockIdx.x * kStepSlots + tid;
     const bool active = env < v.num_envs;
@@ -87,6 +91,55 @@ step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
         dst[q] = make_uint4(*ram_word(slot, 4 * q + 0), *ram_word(slot, 4 * q + 1), *ram_word(slot, 4 * q + 2),
                             *ram_word(slot, 4 * q + 3));
     }
+    const bool faulted = finish_env(v, env, rec, status_before, reward, done, flags & kStepDeviceApi,
+                                    flags & kStepAutoReset);
+    v.rec[env] = rec;
+    if (faulted) atomicAdd(v.fault_count, 1u);
+}
+
+// --------------------------------------------------------------------------
+// Env step, RAM in place.  The env's RAM row stays in global memory (L2
+// resident for moderate batches) and only PRG + decode table are staged, so a
+// CTA is 256 envs and every env of a 65,536-env batch is resident at once:
+// warp parallelism, not shared-memory latency, hides the memory latency.
+// --------------------------------------------------------------------------
+__global__ void __launch_bounds__(kGlobalMaxThreads, 1)
+step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
+                   const long long* __restrict__ act64, uint32_t flags) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* s_prg = smem;
+    Entry* s_dec = reinterpret_cast<Entry*>(smem + kPrgSmem);
+    const BatchView& v = *vp;
+    const uint32_t tid = threadIdx.x;
+    const uint4* prg_src = reinterpret_cast<const uint4*>(v.prg);
+    for (uint32_t i = tid; i < 2048; i += blockDim.x) reinterpret_cast<uint4*>(s_prg)[i] = prg_src[i];
+    if (tid == 0) reinterpret_cast<uint4*>(s_prg)[2048] = make_uint4(0, 0, 0, 0);
+    const uint4* ent_src = reinterpret_cast<const uint4*>(&kEntriesConst);
+    for (uint32_t i = tid; i < kDecSmem / 16; i += blockDim.x) reinterpret_cast<uint4*>(s_dec)[i] = ent_src[i];
+    __syncthreads();
+    const uint32_t env = blockIdx.x * blockDim.x + tid;
+    if (env >= v.num_envs) return;
+
+    Ctx c;
+    c.ram = v.ram + (size_t)env * kRamBytes;
+    c.slots = 1;
+    c.prg = s_prg;
+    c.dec = s_dec;
+    c.view = vp;
+    c.env = env;
+    c.frameskip = v.frameskip;
+    c.max_instr = v.max_instructions;
+    c.prg_ram = v.prg_ram + (size_t)env * kPrgRamBytes;
+    c.nt = v.nt + (size_t)env * kNtBytes;
+    c.pal = v.pal + (size_t)env * kPalBytes;
+    c.oam = v.oam + (size_t)env * kOamBytes;
+
+    EnvRecord rec = v.rec[env];
+    const uint32_t status_before = rec.status;
+    const uint8_t action = act64 ? (uint8_t)(act64[env] & 0xFF) : act8[env];
+    float reward;
+    uint8_t done;
+    run_env_step<false>(c, rec, action, reward, done);
     const bool faulted = finish_env(v, env, rec, status_before, reward, done, flags & kStepDeviceApi,
                                     flags & kStepAutoReset);
     v.rec[env] = rec;
@@ -178,10 +231,26 @@ cudaError_t configure_kernels() {
     return cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)step_smem_bytes());
 }
 
+// Threads per in-place step CTA: one CTA per SM when the batch fits in one
+// wave (65,536 envs on 148 SMs -> 448 threads x 147 CTAs), so every SM holds the
+// same number of warps; larger batches use 448-thread CTAs in several waves.
+uint32_t global_step_threads(uint32_t num_envs, uint32_t num_sms) {
+    const uint32_t per_sm = (num_envs + num_sms - 1) / (num_sms ? num_sms : 1);
+    uint32_t t = (per_sm + 31) / 32 * 32;
+    if (t < 32) t = 32;
+    if (t > kGlobalMaxThreads) t = kGlobalMaxThreads;
+    return t;
+}
+
 cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* act8, const long long* act64,
-                        uint32_t flags, cudaStream_t s) {
-    const uint32_t blocks = (num_envs + kStepSlots - 1) / kStepSlots;
-    step_kernel<<<blocks, kStepSlots, step_smem_bytes(), s>>>(dv, act8, act64, flags);
+                        uint32_t flags, uint32_t variant, uint32_t threads, cudaStream_t s) {
+    if (variant == kStepGlobalRam) {
+        const uint32_t blocks = (num_envs + threads - 1) / threads;
+        step_kernel_global<<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags);
+    } else {
+        const uint32_t blocks = (num_envs + kStepSlots - 1) / kStepSlots;
+        step_kernel<<<blocks, kStepSlots, step_smem_bytes(), s>>>(dv, act8, act64, flags);
+    }
     return cudaGetLastError();
 }
 

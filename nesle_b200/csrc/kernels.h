@@ -8,14 +8,18 @@
 
 namespace nesle {
 
-constexpr uint32_t kStepSlots = 96;  // envs (threads) per step CTA
+constexpr uint32_t kStepSlots = 64;       // envs (threads) per shared-RAM step CTA (multiple of 32: conflict-free banks)
+constexpr uint32_t kGlobalMaxThreads = 448;  // max envs (threads) per in-place step CTA
+
+enum : uint32_t { kStepSharedRam = 0, kStepGlobalRam = 1 };
 
 enum : uint32_t { kStepDeviceApi = 1, kStepAutoReset = 2 };
 
 size_t step_smem_bytes();
 cudaError_t configure_kernels();
+uint32_t global_step_threads(uint32_t num_envs, uint32_t num_sms);
 cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* act8, const long long* act64,
-                        uint32_t flags, cudaStream_t s);
+                        uint32_t flags, uint32_t variant, uint32_t threads, cudaStream_t s);
 cudaError_t launch_reset(const BatchView* dv, uint32_t num_envs, const uint8_t* mask, bool full, cudaStream_t s);
 cudaError_t launch_poke(const BatchView* dv, uint32_t num_envs, uint32_t address, uint32_t value, cudaStream_t s);
 cudaError_t launch_render(const BatchView* dv, uint32_t num_envs, uint8_t* out, int mode, cudaStream_t s);

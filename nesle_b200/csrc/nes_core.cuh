@@ -258,6 +258,100 @@ constexpr DecodeTable build() {
 
 constexpr DecodeTable kDecodeHost = dt::build();
 
+// ---------------------------------------------------------------------------
+// Execution entry: the 64-bit specification word of each opcode expanded into
+// 32 bytes of byte-aligned, ready-to-use masks, so the datapath combines
+// operands with AND/OR instead of extracting fields and chaining selects.
+//   w0: b0 flags0 (E0_*), b1 flags1 (E1_*), b2 length, b3 base cycles
+//   w1: b0 index shift, b1 index mask, b2 (zp,X) add mask, b3 operand-A shift
+//   w2: b0 A-from-register mask, b1 A-from-M mask, b2 A-from-P mask, b3 B-from-M mask
+//   w3: b0 B xor, b1 carry-in (bit0: from C, bit1: one), b2 adder mask, b3 AND mask
+//   w4: b0 XOR mask, b1 shifter mask, b2 P keep mask, b3 P computed mask
+//   w5: b0 P set bits, b1 P-from-result mask, b2 branch flag mask, b3 branch value
+//   w6: register write mask over R = A | X<<8 | Y<<16 | SP<<24
+//   w7: stack-pointer delta added to R (+-1 in the top byte)
+// ---------------------------------------------------------------------------
+enum : uint32_t {
+    E0_RD = 1u << 0, E0_WM = 1u << 1, E0_IMM = 1u << 2, E0_BR = 1u << 3, E0_JMP = 1u << 4,
+    E0_SPECIAL = 1u << 5, E0_ILLEGAL = 1u << 6, E0_PAGE = 1u << 7,
+    E1_STACK = 1u << 8, E1_PULL = 1u << 9, E1_IND = 1u << 10, E1_ZP = 1u << 11, E1_BIT = 1u << 12,
+    E1_SHL = 1u << 13, E1_ROT = 1u << 14,
+};
+
+struct Entry {
+    uint32_t w[8];
+};
+struct EntryTable {
+    Entry e[256];
+};
+
+namespace dt {
+constexpr uint32_t F(uint64_t w, uint32_t pos, uint32_t bits) { return (uint32_t)(w >> pos) & ((1u << bits) - 1u); }
+
+constexpr Entry expand(uint64_t w) {
+    Entry e{};
+    const uint32_t idx = F(w, D_IDX, 2), base = F(w, D_BASE, 2), opa = F(w, D_OPA, 3), unit = F(w, D_UNIT, 3);
+    const uint32_t flg = F(w, D_FLG, 2), fcm = F(w, D_FCM, 8);
+    const bool bit = F(w, D_BIT, 1), wp = F(w, D_WP, 1), br = F(w, D_BR, 1);
+    uint32_t f0 = 0, f1 = 0;
+    f0 |= F(w, D_RD, 1) ? E0_RD : 0u;
+    f0 |= F(w, D_WM, 1) ? E0_WM : 0u;
+    f0 |= F(w, D_IMM, 1) ? E0_IMM : 0u;
+    f0 |= br ? E0_BR : 0u;
+    f0 |= F(w, D_JMP, 1) ? E0_JMP : 0u;
+    f0 |= F(w, D_SPECIAL, 1) ? E0_SPECIAL : 0u;
+    f0 |= F(w, D_ILLEGAL, 1) ? E0_ILLEGAL : 0u;
+    f0 |= F(w, D_PAGE, 1) ? E0_PAGE : 0u;
+    f1 |= base == 3 ? E1_STACK : 0u;
+    f1 |= F(w, D_PULL, 1) ? E1_PULL : 0u;
+    f1 |= base == 2 ? E1_IND : 0u;
+    f1 |= F(w, D_ZPW, 1) ? E1_ZP : 0u;
+    f1 |= bit ? E1_BIT : 0u;
+    f1 |= unit == U_SHL ? E1_SHL : 0u;
+    f1 |= F(w, D_ROT, 1) ? E1_ROT : 0u;
+    const uint32_t len = F(w, D_ILLEGAL, 1) ? 1u : F(w, D_LEN, 2) + 1u;
+    e.w[0] = f0 | f1 | (len << 16) | (F(w, D_CYC, 3) << 24);
+    const uint32_t idx_sh = idx == 1 ? 8u : (idx == 2 ? 16u : 0u);
+    const uint32_t opa_sh = opa == A_X ? 8u : opa == A_Y ? 16u : opa == A_SP ? 24u : 0u;
+    e.w[1] = idx_sh | ((idx ? 0xFFu : 0u) << 8) | ((F(w, D_INDX, 1) ? 0xFFu : 0u) << 16) | (opa_sh << 24);
+    const bool reg = opa <= A_SP;
+    e.w[2] = (reg ? 0xFFu : 0u) | ((opa == A_M ? 0xFFu : 0u) << 8) | ((opa == A_PHP ? 0xFFu : 0u) << 16) |
+             ((F(w, D_BM, 1) ? 0xFFu : 0u) << 24);
+    const uint32_t cin = (F(w, D_CINC, 1) ? 1u : 0u) | (F(w, D_CIN1, 1) ? 2u : 0u);
+    const bool logic_and = unit == U_AND || unit == U_OR, logic_xor = unit == U_XOR || unit == U_OR;
+    e.w[3] = (F(w, D_BX, 1) ? 0xFFu : 0u) | (cin << 8) | ((unit == U_ADD ? 0xFFu : 0u) << 16) |
+             ((logic_and ? 0xFFu : 0u) << 24);
+    uint32_t comp = flg == F_NZ ? 0x82u : flg == F_NZC ? 0x83u : flg == F_NZCV ? 0xC3u : 0u;
+    if (bit) comp = 0xC2u;
+    uint32_t keep = 0xFFu & ~comp & ~fcm;
+    uint32_t set = F(w, D_FCV, 1) ? fcm : 0u;
+    uint32_t from_r = 0;
+    if (flg || bit || fcm) set |= 0x20u;  // set_flag forces the unused bit (cpu.hpp:52-59)
+    if (wp) { keep = 0; comp = 0; from_r = 0xEFu; set |= 0x20u; }  // PLP: (pulled | $20) & ~$10
+    const bool shifter = unit == U_SHL || unit == U_SHR;
+    e.w[4] = (logic_xor ? 0xFFu : 0u) | ((shifter ? 0xFFu : 0u) << 8) | (keep << 16) | (comp << 24);
+    const uint32_t brmask = br ? (1u << F(w, D_BRF, 3)) : 0u;
+    const uint32_t brval = br ? (F(w, D_BRP, 1) ? brmask : 0u) : 0xFFu;  // 0xFF never matches: not a branch
+    e.w[5] = set | (from_r << 8) | (brmask << 16) | (brval << 24);
+    e.w[6] = (F(w, D_WA, 1) ? 0xFFu : 0u) | (F(w, D_WX, 1) ? 0xFF00u : 0u) | (F(w, D_WY, 1) ? 0xFF0000u : 0u) |
+             (F(w, D_WSP, 1) ? 0xFF000000u : 0u);
+    const uint32_t spd = F(w, D_SPD, 2);
+    e.w[7] = spd == 1 ? 0xFF000000u : (spd == 2 ? 0x01000000u : 0u);
+    return e;
+}
+
+constexpr EntryTable build_entries() {
+    EntryTable t{};
+    const DecodeTable d = build();
+    for (int i = 0; i < 256; ++i) t.e[i] = expand(d.e[i]);
+    return t;
+}
+}  // namespace dt
+
+constexpr EntryTable kEntriesHost = dt::build_entries();
+
+NESLE_HD uint32_t byte_of(uint32_t w, uint32_t k) { return (w >> (8 * k)) & 0xFFu; }
+
 NESLE_HD uint32_t dfield(uint64_t d, uint32_t pos, uint32_t bits) {
     return static_cast<uint32_t>(d >> pos) & ((1u << bits) - 1u);
 }
@@ -283,7 +377,7 @@ NESLE_HD uint32_t frame_limit(const BatchView& v, uint32_t env, uint32_t episode
 // Lane state: every scalar of the env, register-resident during a launch.
 // ---------------------------------------------------------------------------
 struct Lane {
-    uint32_t pc, a, x, y, sp, p;
+    uint32_t pc, R, p;  // R = A | X<<8 | Y<<16 | SP<<24
     uint64_t cycles;
     uint64_t frame;
     uint32_t frame_dot, ctrl, mask, status, nmi;
@@ -300,7 +394,8 @@ struct Lane {
 };
 
 NESLE_HD void load_lane(Lane& L, const EnvRecord& r, uint8_t action) {
-    L.pc = r.pc; L.a = r.a; L.x = r.x; L.y = r.y; L.sp = r.sp; L.p = r.p;
+    L.pc = r.pc; L.p = r.p;
+    L.R = (uint32_t)r.a | ((uint32_t)r.x << 8) | ((uint32_t)r.y << 16) | ((uint32_t)r.sp << 24);
     L.cycles = r.cycles; L.frame = r.frame; L.frame_dot = r.frame_dot;
     L.ctrl = r.ppu_ctrl; L.mask = r.ppu_mask; L.status = r.ppu_status; L.nmi = r.nmi_pending;
     L.oam_addr = r.oam_addr; L.v = r.v; L.t = r.t; L.fine_x = r.fine_x; L.w = r.w;
@@ -315,8 +410,8 @@ NESLE_HD void load_lane(Lane& L, const EnvRecord& r, uint8_t action) {
 }
 
 NESLE_HD void store_lane(const Lane& L, EnvRecord& r) {
-    r.pc = (uint16_t)L.pc; r.a = (uint8_t)L.a; r.x = (uint8_t)L.x; r.y = (uint8_t)L.y;
-    r.sp = (uint8_t)L.sp; r.p = (uint8_t)L.p; r.nmi_pending = (uint8_t)L.nmi;
+    r.pc = (uint16_t)L.pc; r.a = (uint8_t)L.R; r.x = (uint8_t)(L.R >> 8); r.y = (uint8_t)(L.R >> 16);
+    r.sp = (uint8_t)(L.R >> 24); r.p = (uint8_t)L.p; r.nmi_pending = (uint8_t)L.nmi;
     r.cycles = L.cycles; r.frame = L.frame; r.frame_dot = L.frame_dot;
     r.ppu_ctrl = (uint8_t)L.ctrl; r.ppu_mask = (uint8_t)L.mask; r.ppu_status = (uint8_t)L.status;
     r.oam_addr = (uint8_t)L.oam_addr; r.v = (uint16_t)L.v; r.t = (uint16_t)L.t;
@@ -341,7 +436,7 @@ struct Ctx {
     uint8_t* ram;         // &smem_ram[slot * 4]; byte a at ram[(a & 0x7FC) * slots + (a & 3)]
     uint32_t slots;       // RAM slots per CTA (interleave stride / 4)
     const uint8_t* prg;   // 32 KB (shared)
-    const uint64_t* dec;  // decode table (shared)
+    const Entry* dec;     // execution entries (shared)
     const BatchView* view;
     uint32_t env;
     uint32_t frameskip;   // copies of view fields read on every iteration
@@ -543,8 +638,14 @@ NESLE_HD void io_wr(const Ctx& c, Lane& L, uint32_t a, uint32_t val) {
 NESLE_HD bool fast_read(uint32_t a) { return a < 0x2000 || a >= 0x8000; }
 NESLE_HD bool fast_write(uint32_t a) { return a < 0x2000; }
 
-NESLE_HD void push8(const Ctx& c, Lane& L, uint32_t v) { ram_wr(c, 0x100 | L.sp, v); L.sp = (L.sp - 1) & 0xFF; }
-NESLE_HD uint32_t pull8(const Ctx& c, Lane& L) { L.sp = (L.sp + 1) & 0xFF; return ram_rd(c, 0x100 | L.sp); }
+NESLE_HD void push8(const Ctx& c, Lane& L, uint32_t v) {
+    ram_wr(c, 0x100 | (L.R >> 24), v);
+    L.R -= 0x01000000u;
+}
+NESLE_HD uint32_t pull8(const Ctx& c, Lane& L) {
+    L.R += 0x01000000u;
+    return ram_rd(c, 0x100 | (L.R >> 24));
+}
 
 // cpu.hpp:112-123
 NESLE_HD void nmi_entry(const Ctx& c, Lane& L) {
@@ -553,7 +654,6 @@ NESLE_HD void nmi_entry(const Ctx& c, Lane& L) {
     push8(c, L, (L.p & ~0x10u) | 0x20u);
     L.p |= 0x24;
     L.pc = c.prg[0x7FFA] | (c.prg[0x7FFB] << 8);
-    L.cycles += 7;
 }
 
 // ---------------------------------------------------------------------------
@@ -664,6 +764,8 @@ NESLE_HD void exec_special(const Ctx& c, Lane& L, uint32_t op, uint32_t b1, uint
     }
 }
 
+
+
 #if defined(__CUDA_ARCH__)
 #define NESLE_FUNNEL(lo, hi, s) __funnelshift_r((lo), (hi), (s))
 #else
@@ -671,139 +773,157 @@ NESLE_HD void exec_special(const Ctx& c, Lane& L, uint32_t op, uint32_t b1, uint
 #endif
 
 // ---------------------------------------------------------------------------
-// One instruction on the uniform datapath: cpu.hpp:378-730 restated as data
-// flow.  Returns the opcode, or -1 when the env froze (status word set).
+// Instruction fetch.  The instruction at the next PC is fetched and decoded
+// while the current one executes (its PC is known before its data path runs:
+// flags for branches come from the previous instruction).  PRG ROM cannot be
+// written, so a fetch from the shared PRG window is exact whenever it happens;
+// every other fetch goes through the bus when the instruction starts.
 // ---------------------------------------------------------------------------
-NESLE_HD int exec_instruction(const Ctx& c, Lane& L) {
-    const uint32_t pc = L.pc;
+struct Fetched {
     uint32_t op, b1, b2;
-    if (pc - 0x8000u <= 0x7FFDu) {
-        const uint32_t wi = (pc & 0x7FFF) >> 2;
-        const uint32_t* p32 = reinterpret_cast<const uint32_t*>(c.prg);
-        const uint32_t bytes = NESLE_FUNNEL(p32[wi], p32[wi + 1], (pc & 3) * 8);
-        op = bytes & 0xFF;
-        b1 = (bytes >> 8) & 0xFF;
-        b2 = (bytes >> 16) & 0xFF;
-    } else {
-        // Outside the shared PRG window (code in RAM, PRG-RAM or I/O space, or
-        // an instruction running past $FFFF): fetch the bytes this opcode
-        // uses through the full bus, in order, as cpu.hpp:382-392 does.
-        op = io_rd(c, L, pc);
-        const uint64_t dd = c.dec[op];
-        const uint32_t len = (dd & (1ull << D_ILLEGAL)) ? 0u : dfield(dd, D_LEN, 2);
-        b1 = len >= 1 ? io_rd(c, L, (pc + 1) & 0xFFFF) : 0u;
-        b2 = len >= 2 ? io_rd(c, L, (pc + 2) & 0xFFFF) : 0u;
-    }
-    const uint64_t d = c.dec[op];
-    if (d & (1ull << D_ILLEGAL)) {
-        L.status_word = NESLE_STATUS_ILLEGAL | (op << 16) | pc;
-        return -1;
-    }
-    const uint32_t len = dfield(d, D_LEN, 2) + 1;
-    uint32_t cyc = dfield(d, D_CYC, 3);
-    if (d & (1ull << D_SPECIAL)) {
-        exec_special(c, L, op, b1, b2);
-        L.cycles += cyc;
-        return (int)op;
-    }
+    Entry e;
+};
+
+NESLE_HD bool in_prg_window(uint32_t pc) { return pc - 0x8000u <= 0x7FFDu; }
+
+NESLE_HD void load_entry(const Ctx& c, uint32_t op, Entry& e) {
+#if defined(__CUDA_ARCH__)
+    const uint4* src = reinterpret_cast<const uint4*>(&c.dec[op]);
+    const uint4 a = src[0], b = src[1];
+    e.w[0] = a.x; e.w[1] = a.y; e.w[2] = a.z; e.w[3] = a.w;
+    e.w[4] = b.x; e.w[5] = b.y; e.w[6] = b.z; e.w[7] = b.w;
+#else
+    e = c.dec[op];
+#endif
+}
+
+// Memory-safe for any pc (the shared PRG copy carries one padding word);
+// meaningful only when in_prg_window(pc).
+NESLE_HD void fetch_prg(const Ctx& c, uint32_t pc, Fetched& f) {
+    const uint32_t wi = (pc & 0x7FFF) >> 2;
+    const uint32_t* p32 = reinterpret_cast<const uint32_t*>(c.prg);
+    const uint32_t bytes = NESLE_FUNNEL(p32[wi], p32[wi + 1], (pc & 3) * 8);
+    f.op = bytes & 0xFF;
+    f.b1 = (bytes >> 8) & 0xFF;
+    f.b2 = (bytes >> 16) & 0xFF;
+    load_entry(c, f.op, f.e);
+}
+
+// Fetch through the bus, only the bytes the opcode uses, in order
+// (cpu.hpp:382-392, 566-587): code in RAM, PRG-RAM or I/O space.
+NESLE_HD void fetch_bus(const Ctx& c, Lane& L, Fetched& f) {
+    f.op = io_rd(c, L, L.pc);
+    load_entry(c, f.op, f.e);
+    const uint32_t len = byte_of(f.e.w[0], 2);  // 1 for illegal opcodes
+    f.b1 = len >= 2 ? io_rd(c, L, (L.pc + 1) & 0xFFFF) : 0u;
+    f.b2 = len >= 3 ? io_rd(c, L, (L.pc + 2) & 0xFFFF) : 0u;
+}
+
+// ---------------------------------------------------------------------------
+// One instruction on the uniform datapath: cpu.hpp:378-730 restated as data
+// flow over the opcode's execution entry.  Straight-line except for the rare
+// I/O side paths; shared-memory loads are unconditional where cheap and
+// results are merged with table masks, so lanes at different opcodes stay
+// converged.  Returns the instruction's cycles; on return `f` holds the next
+// instruction and `fresh` says whether it is valid.
+// kSharedRam: the env's RAM sits in the interleaved shared-memory slot;
+// otherwise it is the env's row in global memory and loads are predicated.
+// ---------------------------------------------------------------------------
+template <bool kSharedRam>
+NESLE_HD uint32_t exec_uniform(const Ctx& c, Lane& L, Fetched& f, bool& fresh) {
+    const uint32_t pc = L.pc, b1 = f.b1, b2 = f.b2, R = L.R, P = L.p;
+    const uint32_t w0 = f.e.w[0], w1 = f.e.w[1], w2 = f.e.w[2], w3 = f.e.w[3], w4 = f.e.w[4], w5 = f.e.w[5];
+    const uint32_t wmask = f.e.w[6], spd = f.e.w[7];
+    const uint32_t b16 = b1 | (b2 << 8);
+
+    // ---- next PC (flags from the previous instruction), then prefetch it ----
+    const uint32_t seq = (pc + byte_of(w0, 2)) & 0xFFFF;
+    const uint32_t target = (seq + (uint32_t)(int32_t)(int8_t)b1) & 0xFFFF;
+    const bool taken = (P & byte_of(w5, 2)) == byte_of(w5, 3);
+    uint32_t npc = taken ? target : seq;
+    npc = (w0 & E0_JMP) ? b16 : npc;
+    uint32_t cyc = byte_of(w0, 3) + (taken ? 1u + (((seq ^ target) & 0xFF00u) ? 1u : 0u) : 0u);
+    Fetched nf;
+    fetch_prg(c, npc, nf);
 
     // ---- effective address ----
-    const uint32_t idx_sel = dfield(d, D_IDX, 2);
-    const uint32_t idx = idx_sel == 1 ? L.x : (idx_sel == 2 ? L.y : 0u);
-    const uint32_t base_sel = dfield(d, D_BASE, 2);
-    uint32_t base = base_sel == 0 ? b1 : (b1 | (b2 << 8));
-    if (base_sel == 2) {  // (zp,X) / (zp),Y pointer from zero page
-        const uint32_t ptr = (b1 + ((d >> D_INDX) & 1 ? L.x : 0u)) & 0xFF;
-        base = ram_rd(c, ptr) | (ram_rd(c, (ptr + 1) & 0xFF) << 8);
-    }
-    uint32_t addr = (base + idx) & 0xFFFF;
-    if ((d >> D_ZPW) & 1) addr &= 0xFF;
-    if ((d >> D_PAGE) & 1) cyc += ((base ^ addr) & 0xFF00) ? 1u : 0u;
-    if (base_sel == 3) addr = 0x100 | ((L.sp + ((d >> D_PULL) & 1)) & 0xFF);
+    const uint32_t idx = (R >> byte_of(w1, 0)) & byte_of(w1, 1);
+    const uint32_t zp = (b1 + ((R >> 8) & byte_of(w1, 2))) & 0xFF;
+    const bool ind = (w0 & E1_IND) != 0;
+    uint32_t ptr = 0;
+    if (kSharedRam || ind) ptr = ram_rd(c, zp) | (ram_rd(c, (zp + 1) & 0xFF) << 8);
+    const uint32_t wrap = (w0 & E1_ZP) ? 0xFFu : 0xFFFFu;
+    const uint32_t base = ind ? ptr : (b16 & wrap);
+    uint32_t addr = (base + idx) & wrap;
+    cyc += ((w0 & E0_PAGE) && ((base ^ addr) & 0xFF00u)) ? 1u : 0u;
+    addr = (w0 & E1_STACK) ? (0x100u | (((R >> 24) + ((w0 >> 9) & 1u)) & 0xFFu)) : addr;
 
-    // ---- operand read ----
-    uint32_t m = b1;  // immediate
-    if ((d >> D_RD) & 1) {
-        if (fast_read(addr)) {
-            m = addr < 0x2000 ? c.ram[ram_off(c, addr)] : c.prg[addr & 0x7FFF];
-        } else {
-            m = io_rd(c, L, addr);
-        }
+    // ---- operand read: RAM/PRG from fast memory, $4016/$4017 and the
+    //      unmapped $4000-$5FFF reads inline, PPU registers and PRG-RAM aside ----
+    const bool rd = (w0 & E0_RD) != 0, wm = (w0 & E0_WM) != 0;
+    const bool is_ram = addr < 0x2000u, is_prg = addr >= 0x8000u, is_ctrl = addr == 0x4016u;
+    uint8_t* ram_byte = c.ram + ram_off(c, addr);
+    uint32_t mem;
+    if (kSharedRam) {
+        const uint8_t* src = is_ram ? ram_byte : c.prg + (addr & 0x7FFF);
+        mem = *src;
+    } else {
+        mem = c.prg[addr & 0x7FFF];
+        if (rd && is_ram) mem = *ram_byte;
     }
+    const uint32_t cbit = L.cstrobe ? (L.action & 1u) : (L.ccount < 8 ? (L.cshift & 1u) : 1u);
+    uint32_t m = (is_ram || is_prg) ? mem : (is_ctrl ? (0x40u | cbit) : (addr == 0x4017u ? 0x41u : 0u));
+    m = (w0 & E0_IMM) ? b1 : m;
+    const bool io_space = (addr - 0x2000u < 0x2000u) || (addr - 0x6000u < 0x2000u);
+    bool side = false;
+    if (rd && io_space) {
+        m = io_rd(c, L, addr);
+        side = true;
+    }
+    const bool shift_now = rd && is_ctrl && !L.cstrobe && L.ccount < 8;  // batch_bus.cuh:115-121
+    L.cshift = shift_now ? (L.cshift >> 1) : L.cshift;
+    L.ccount += shift_now ? 1u : 0u;
 
-    // ---- ALU ----
-    const uint32_t opa_sel = dfield(d, D_OPA, 3);
-    uint32_t opa;
-    switch (opa_sel) {
-        case A_A: opa = L.a; break;
-        case A_X: opa = L.x; break;
-        case A_Y: opa = L.y; break;
-        case A_SP: opa = L.sp; break;
-        case A_M: opa = m; break;
-        case A_PHP: opa = L.p | 0x30; break;
-        default: opa = 0; break;
-    }
-    const uint32_t carry_in = ((d >> D_CINC) & 1) ? (L.p & 1) : ((d >> D_CIN1) & 1);
-    const uint32_t opb = (((d >> D_BM) & 1) ? m : 0u) ^ (((d >> D_BX) & 1) ? 0xFFu : 0u);
-    const uint32_t sum = opa + opb + carry_in;
-    const uint32_t unit = dfield(d, D_UNIT, 3);
-    const uint32_t rot_c = ((d >> D_ROT) & 1) ? (L.p & 1) : 0u;
-    uint32_t r, cout;
-    switch (unit) {
-        case U_AND: r = opa & m; cout = 0; break;
-        case U_OR: r = opa | m; cout = 0; break;
-        case U_XOR: r = opa ^ m; cout = 0; break;
-        case U_SHL: r = ((opa << 1) | rot_c) & 0xFF; cout = opa >> 7; break;
-        case U_SHR: r = (opa >> 1) | (rot_c << 7); cout = opa & 1; break;
-        default: r = sum & 0xFF; cout = (sum >> 8) & 1; break;
-    }
+    // ---- ALU: operands and units merged through the entry's masks ----
+    const uint32_t opa = ((R >> byte_of(w1, 3)) & byte_of(w2, 0)) | (m & byte_of(w2, 1)) |
+                         ((P | 0x30u) & byte_of(w2, 2));
+    const uint32_t opb = (m & byte_of(w2, 3)) ^ byte_of(w3, 0);
+    const uint32_t cinb = byte_of(w3, 1);
+    const uint32_t sum = opa + opb + ((P & cinb & 1u) | (cinb >> 1));
+    const uint32_t rotc = (w0 & E1_ROT) ? (P & 1u) : 0u;
+    const bool shl = (w0 & E1_SHL) != 0;
+    const uint32_t rsh = shl ? (((opa << 1) | rotc) & 0xFFu) : ((opa >> 1) | (rotc << 7));
+    const uint32_t csh = shl ? (opa >> 7) : (opa & 1u);
+    const uint32_t kadd = byte_of(w3, 2), kand = byte_of(w3, 3), kxor = byte_of(w4, 0), ksh = byte_of(w4, 1);
+    const uint32_t r = (sum & kadd) | (opa & m & kand) | ((opa ^ m) & kxor) | (rsh & ksh);
+    const uint32_t cout = (((sum >> 8) & kadd) | (csh & ksh)) & 1u;
 
-    // ---- flags ----
-    const uint32_t flg = dfield(d, D_FLG, 2);
-    uint32_t p = L.p;
-    if (flg) {
-        uint32_t mask = 0x82, val = (r & 0x80) | (r == 0 ? 0x02u : 0u);
-        if (flg >= F_NZC) { mask |= 0x01; val |= cout; }
-        if (flg == F_NZCV) { mask |= 0x40; val |= ((~(opa ^ opb) & (opa ^ r)) & 0x80) ? 0x40u : 0u; }
-        p = (p & ~mask) | val;
-    }
-    if ((d >> D_BIT) & 1) p = (p & ~0xC2u) | (m & 0xC0) | (r == 0 ? 0x02u : 0u);
-    const uint32_t fcm = dfield(d, D_FCM, 8);
-    p = (p & ~fcm) | (((d >> D_FCV) & 1) ? fcm : 0u);
-    if ((d >> D_WP) & 1) p = (r | 0x20) & ~0x10u;
-    // The reference forces the unused bit only when an instruction writes a
-    // flag (set_flag, cpu.hpp:52-59); stores, branches and jumps leave P as is.
-    if (flg | ((d >> D_BIT) & 1) | fcm) p |= 0x20;
+    // ---- flags: P = (P & keep) | (computed & comp) | set | (r & from_r) ----
+    const uint32_t zbit = r == 0 ? 0x02u : 0u;
+    const uint32_t vbit = ((~(opa ^ opb) & (opa ^ r)) >> 1) & 0x40u;
+    const uint32_t nv = (w0 & E1_BIT) ? (m & 0xC0u) : ((r & 0x80u) | vbit);
+    const uint32_t p = (P & byte_of(w4, 2)) | ((nv | zbit | cout) & byte_of(w4, 3)) | byte_of(w5, 0) |
+                       (r & byte_of(w5, 1));
 
     // ---- memory write ----
-    if ((d >> D_WM) & 1) {
-        if (fast_write(addr)) c.ram[ram_off(c, addr)] = (uint8_t)r;
-        else io_wr(c, L, addr, r);
+    if (wm && is_ram) *ram_byte = (uint8_t)r;
+    const bool cw = wm && is_ctrl;  // $4016 strobe (batch_bus.cuh:125-133)
+    const bool latch = cw && ((r & 1u) || L.cstrobe);
+    L.cshift = latch ? L.action : L.cshift;
+    L.ccount = latch ? 0u : L.ccount;
+    L.cstrobe = cw ? (r & 1u) : L.cstrobe;
+    if (wm && (io_space || addr == 0x4014u)) {
+        io_wr(c, L, addr, r);
+        side = true;
     }
 
     // ---- register write-back ----
-    if ((d >> D_WA) & 1) L.a = r;
-    if ((d >> D_WX) & 1) L.x = r;
-    if ((d >> D_WY) & 1) L.y = r;
-    if ((d >> D_WSP) & 1) L.sp = r;
-    const uint32_t spd = dfield(d, D_SPD, 2);
-    if (spd) L.sp = (L.sp + (spd == 1 ? 0xFFu : 1u)) & 0xFF;
-
-    // ---- next PC ----
-    uint32_t npc = pc + len;
-    if ((d >> D_BR) & 1) {
-        const uint32_t flag = (L.p >> dfield(d, D_BRF, 3)) & 1;  // flags before this instruction
-        if (flag == ((d >> D_BRP) & 1)) {
-            const uint32_t target = (npc + (uint32_t)(int32_t)(int8_t)b1) & 0xFFFF;
-            cyc += 1 + (((npc ^ target) & 0xFF00) ? 1u : 0u);
-            npc = target;
-        }
-    }
-    if ((d >> D_JMP) & 1) npc = b1 | (b2 << 8);
+    L.R = ((R & ~wmask) | ((r * 0x01010101u) & wmask)) + spd;
     L.p = p;
-    L.pc = npc & 0xFFFF;
-    L.cycles += cyc;
-    return (int)op;
+    L.pc = npc;
+    f = nf;
+    fresh = in_prg_window(npc) && !side;
+    return cyc;
 }
 
 // ---------------------------------------------------------------------------
@@ -844,34 +964,16 @@ NESLE_HD bool loop_top(const Ctx& c, Lane& L) {
     }
 }
 
-// One loop iteration after loop_top() returned true:
-// step_batch_console_instruction_lazy (batch_console.hpp:77-109) plus the idle
-// fast-forward (kernels.cu:66-76, batch_console.hpp:129-152).
-NESLE_HD void step_once(const Ctx& c, Lane& L) {
-    const uint64_t before = L.cycles;
-    if (L.nmi) {
-        L.nmi = 0;
-        nmi_entry(c, L);
+// JMP-to-self fast-forward (kernels.cu:66-76, batch_console.hpp:129-152).
+NESLE_HD void idle_fast_forward(const Ctx& c, Lane& L) {
+    L.fcomp += settle(c, L, L.pending);
+    L.pending = 0;
+    const uint32_t jumps = (next_event(L) + 8u) / 9u;
+    if (jumps) {
+        L.cycles += (uint64_t)jumps * 3u;
+        L.fcomp += settle(c, L, jumps * 9u);
     }
-    const uint32_t op_pc = L.pc;
-    const int op = exec_instruction(c, L);
-    if (op < 0) return;  // frozen: loop_top ends the frame
-    if (L.dma) {
-        L.cycles += L.dma;
-        L.dma = 0;
-    }
-    L.pending += (uint32_t)(L.cycles - before) * 3u;
-    L.instr++;
-    if (op == 0x4C && L.pc == op_pc && L.fcomp == 0) {
-        L.fcomp += settle(c, L, L.pending);
-        L.pending = 0;
-        const uint32_t jumps = (next_event(L) + 8u) / 9u;
-        if (jumps) {
-            L.cycles += (uint64_t)jumps * 3u;
-            L.fcomp += settle(c, L, jumps * 9u);
-        }
-        L.horizon = next_event(L);
-    }
+    L.horizon = next_event(L);
 }
 
 NESLE_HD void begin_step(Lane& L) {
@@ -883,6 +985,56 @@ NESLE_HD void begin_step(Lane& L) {
     L.tot_instr = 0;
     L.tot_frames = 0;
     L.budget = 0;
+}
+
+// All frames of one env-step: step_batch_console_instruction_lazy
+// (batch_console.hpp:77-109) per iteration, with the loop-top bookkeeping,
+// NMI entry and bus fetches on the rare path.
+template <bool kSharedRam>
+NESLE_HD void run_frames(const Ctx& c, Lane& L) {
+    Fetched f{};
+    bool fresh = false;
+    for (;;) {
+        uint32_t it_cyc = 0;
+        if (!fresh || L.pending >= L.horizon || L.instr >= c.max_instr) {
+            if (!loop_top(c, L)) break;
+            if (L.nmi) {
+                L.nmi = 0;
+                nmi_entry(c, L);
+                it_cyc = 7;
+                fresh = false;
+            }
+            if (!fresh) {
+                if (in_prg_window(L.pc)) fetch_prg(c, L.pc, f);
+                else fetch_bus(c, L, f);
+                fresh = true;
+            }
+        }
+        const uint32_t pc = L.pc, op = f.op;
+        if (f.e.w[0] & (E0_SPECIAL | E0_ILLEGAL)) {
+            if (f.e.w[0] & E0_ILLEGAL) {
+                // The reference executes `trap` (cpu.hpp:716-720); the env stops instead.
+                L.status_word = NESLE_STATUS_ILLEGAL | (op << 16) | pc;
+                L.cycles += it_cyc;
+                fresh = false;
+                continue;
+            }
+            exec_special(c, L, op, f.b1, f.b2);
+            it_cyc += byte_of(f.e.w[0], 3);
+            fresh = false;
+        } else {
+            it_cyc += exec_uniform<kSharedRam>(c, L, f, fresh);
+        }
+        it_cyc += L.dma;
+        L.dma = 0;
+        L.cycles += it_cyc;
+        L.pending += it_cyc * 3u;
+        L.instr++;
+        if (op == 0x4C && L.pc == pc && L.fcomp == 0) {
+            idle_fast_forward(c, L);
+            fresh = false;
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -993,11 +1145,12 @@ NESLE_HD void seed_presentation(const BatchView& v, uint32_t env, EnvRecord& r) 
 
 // Runs env `c.env` for one env-step (frameskip frames).  Its RAM must be
 // staged at `c.ram`; `rec` is updated in place.
+template <bool kSharedRam = true>
 NESLE_HD void run_env_step(const Ctx& c, EnvRecord& rec, uint8_t action, float& reward, uint8_t& done) {
     Lane L;
     load_lane(L, rec, action);
     begin_step(L);
-    while (loop_top(c, L)) step_once(c, L);
+    run_frames<kSharedRam>(c, L);
     reward_done(c, L, reward, done);
     store_lane(L, rec);
 }

@@ -58,6 +58,7 @@ class _Common:
 
 class HostCore(_Common):
     _h_lib = None
+    global_ram = False  # subclass HostCoreGlobal runs the in-place RAM variant
 
     @classmethod
     def lib(cls):
@@ -72,6 +73,7 @@ class HostCore(_Common):
             lib.host_step.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
             lib.host_render.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
             lib.host_copy_field.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_uint64]
+            lib.host_set_global_ram.argtypes = [ctypes.c_void_p, ctypes.c_int]
             cls._h_lib = lib
         return cls._h_lib
 
@@ -84,6 +86,7 @@ class HostCore(_Common):
         if self.lib().host_create(ctypes.byref(args), ctypes.byref(h)):
             raise ValueError(self.lib().host_last_error().decode())
         self._h = h
+        self.lib().host_set_global_ram(h, int(self.global_ram))
 
     def __del__(self):
         if getattr(self, "_h", None):
@@ -116,6 +119,10 @@ class HostCore(_Common):
         rc = self.lib().host_copy_field(self._h, name.encode(), out.ctypes.data, out.nbytes)
         if rc:
             raise KeyError(self.lib().host_last_error().decode())
+
+
+class HostCoreGlobal(HostCore):
+    global_ram = True
 
 
 class GpuCore(_Common):

@@ -31,6 +31,7 @@ struct HostBatch {
     std::vector<BankRecord> bank;
     std::vector<uint8_t> bram, bprg, bnt, bpal, boam, e2l;
     uint32_t fault = 0;
+    bool global_ram = false;  // run the in-place (global-RAM) variant of the core
     std::vector<uint8_t> smem_ram = std::vector<uint8_t>(kSlots * kRamBytes);
 };
 
@@ -111,6 +112,8 @@ int host_create(const nesle_create_args* a, void** out) {
 
 void host_destroy(void* p) { delete static_cast<HostBatch*>(p); }
 
+void host_set_global_ram(void* p, int on) { static_cast<HostBatch*>(p)->global_ram = on != 0; }
+
 void host_reset(void* p) {
     auto* h = static_cast<HostBatch*>(p);
     for (uint32_t e = 0; e < h->v.num_envs; ++e) {
@@ -139,14 +142,14 @@ void host_poke_ram(void* p, uint16_t address, uint8_t value) {
 
 void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) {
     auto* h = static_cast<HostBatch*>(p);
-    uint64_t dec[256];
-    memcpy(dec, kDecodeHost.e, sizeof(dec));
+    static const EntryTable& dec_table = kEntriesHost;
+    const Entry* dec = dec_table.e;
     for (uint32_t e = 0; e < h->v.num_envs; ++e) {
         const uint32_t slot = e % kSlots;
-        stage(*h, e, slot);
+        if (!h->global_ram) stage(*h, e, slot);
         Ctx c;
-        c.ram = h->smem_ram.data() + slot * 4;
-        c.slots = kSlots;
+        c.ram = h->global_ram ? h->ram.data() + (size_t)e * kRamBytes : h->smem_ram.data() + slot * 4;
+        c.slots = h->global_ram ? 1 : kSlots;
         c.prg = h->prg.data();
         c.dec = dec;
         c.view = &h->v;
@@ -161,8 +164,12 @@ void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) 
         const uint32_t before = rec.status;
         float reward;
         uint8_t done;
-        run_env_step(c, rec, actions[e], reward, done);
-        unstage(*h, e, slot);
+        if (h->global_ram) {
+            run_env_step<false>(c, rec, actions[e], reward, done);
+        } else {
+            run_env_step<true>(c, rec, actions[e], reward, done);
+            unstage(*h, e, slot);
+        }
         if (finish_env(h->v, e, rec, before, reward, done, device_api != 0, auto_reset != 0)) h->fault++;
         h->rec[e] = rec;
     }

@@ -6,14 +6,14 @@ import numpy as np
 import pytest
 
 import kat_roms as kat
-from harness import STATE_FIELDS, HostCore, assert_same, run_lockstep
+from harness import STATE_FIELDS, HostCore, HostCoreGlobal, assert_same, run_lockstep
 from nesle_b200 import workloads as w
 from oracle import Oracle
 
 
 @pytest.mark.parametrize("make,auto_reset", [(w.config1, False), (w.config2, True), (w.config4, True)])
 def test_configs_lockstep(make, auto_reset):
-    run_lockstep(make, 8, 8, auto_reset, [HostCore])
+    run_lockstep(make, 8, 8, auto_reset, [HostCore, HostCoreGlobal])
 
 
 def test_frame_limit_auto_reset_lockstep():
@@ -21,7 +21,7 @@ def test_frame_limit_auto_reset_lockstep():
         wl = w.config4()
         wl.done_args = (5, 17)
         return wl
-    _, _, dones = run_lockstep(short, 12, 20, True, [HostCore])
+    _, _, dones = run_lockstep(short, 12, 20, True, [HostCore, HostCoreGlobal])
     assert dones > 10
 
 
@@ -78,14 +78,15 @@ def test_every_official_opcode_from_random_state(seed):
     """Each official opcode once from a random register/flag/RAM state (P bit 5 may be clear)."""
     for opc, rom, snap in _single_instruction_cases(seed, 1):
         o = Oracle(1, 1, rom, [snap])
-        h = HostCore(1, 1, rom, [snap])
+        sims = [HostCore(1, 1, rom, [snap]), HostCoreGlobal(1, 1, rom, [snap])]
         a = np.zeros(1, np.uint8)
         o.step(a, auto_reset=False)
-        h.step(a, auto_reset=False)
-        try:
-            assert_same(o, h, ("pc", "a", "x", "y", "sp", "p", "cycles", "ram", "prg_ram", "status"))
-        except AssertionError as e:
-            raise AssertionError(f"opcode {opc:#04x}: {e}") from None
+        for h in sims:
+            h.step(a, auto_reset=False)
+            try:
+                assert_same(o, h, ("pc", "a", "x", "y", "sp", "p", "cycles", "ram", "prg_ram", "status"))
+            except AssertionError as e:
+                raise AssertionError(f"opcode {opc:#04x} ({type(h).__name__}): {e}") from None
 
 
 def render_snapshots(seed: int, k: int, pc: int) -> list[bytes]:

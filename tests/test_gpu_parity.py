@@ -29,8 +29,11 @@ def _cuda():
 
 @pytest.mark.parametrize("make,auto_reset,n", [(w.config1, False, 64), (w.config2, True, 200),
                                                (w.config4, True, 200)])
-def test_configs_lockstep(make, auto_reset, n):
-    """Every step, every field, against the checker (200 envs = 2 full CTAs + a partial one)."""
+@pytest.mark.parametrize("variant", ["shared", "global"])
+def test_configs_lockstep(make, auto_reset, n, variant, monkeypatch):
+    """Every step, every field, against the checker (200 envs = 2 full CTAs + a partial one),
+    for both placements of env RAM in the step kernel."""
+    monkeypatch.setenv("NESLE_STEP_KERNEL", variant)
     run_lockstep(make, n, 6, auto_reset, [GpuCore])
 
 
