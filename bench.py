@@ -110,6 +110,11 @@ class ClockSampler:
             self.thread.start()
         except (FileNotFoundError, OSError):
             self.proc = None
+            return self
+        # nvidia-smi's start-up can delay kernel launches; time only once it reports.
+        t0 = time.perf_counter()
+        while not self.lines and self.proc.poll() is None and time.perf_counter() - t0 < 10.0:
+            time.sleep(0.05)
         return self
 
     def _read(self):
@@ -169,12 +174,13 @@ def reference_cpu_rate(wl, envs_total: int, steps: int, warmup: int, budget_s: f
             return Reference("A", n, wl.frameskip, wl.rom.image, wl.snapshots, threads=threads, **kw), env
         return Oracle(n, wl.frameskip, wl.rom.image, wl.snapshots, **kw), env
 
-    # calibrate: one step of `threads` envs
+    # calibrate: one warm step of `threads` envs (after a first step that pays thread start-up)
     sim, env = make(sample_envs, 0)
-    t0 = time.perf_counter()
     sim.step(wl.actions(env, 0))
+    t0 = time.perf_counter()
+    sim.step(wl.actions(env, 1))
     dt = time.perf_counter() - t0
-    per_step_budget = budget_s / max(1, steps + warmup)
+    per_step_budget = budget_s / max(1, steps)
     scale = max(1, int(per_step_budget / max(dt, 1e-6)))
     sample_envs = min(envs_total, sample_envs * scale)
     sample_envs = max(threads, (sample_envs // threads) * threads)
@@ -342,7 +348,8 @@ def run_reference(args, rank, world, local) -> dict | None:
                               budget_s=min(120.0, 6.0 * (args.steps + args.warmup)))
     return {
         "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": 1e3 * base["seconds"] / args.steps, "higher_is_better": True,
+        "scaling": "weak",
         "vs_baseline": None, "dtype": "u8", "data": "synthetic", "impl": "reference",
         "config": workload_config(wl, args.envs, world),
         "cpu_baseline": base,
