@@ -164,7 +164,6 @@ def reference_cpu_rate(wl, envs_total: int, steps: int, warmup: int, budget_s: f
 
     threads = host_threads()
     kind = "reference" if reference_available() else "port"
-    sample_envs = max(threads, 8)
 
     def make(n, offset):
         env = np.arange(offset, offset + n)
@@ -174,16 +173,20 @@ def reference_cpu_rate(wl, envs_total: int, steps: int, warmup: int, budget_s: f
             return Reference("A", n, wl.frameskip, wl.rom.image, wl.snapshots, threads=threads, **kw), env
         return Oracle(n, wl.frameskip, wl.rom.image, wl.snapshots, **kw), env
 
-    # calibrate: one warm step of `threads` envs (after a first step that pays thread start-up)
-    sim, env = make(sample_envs, 0)
-    sim.step(wl.actions(env, 0))
-    t0 = time.perf_counter()
-    sim.step(wl.actions(env, 1))
-    dt = time.perf_counter() - t0
+    # calibrate: grow the sample until one warm step fills its share of the budget
+    # (small samples are dominated by per-step thread start-up)
     per_step_budget = budget_s / max(1, steps)
-    scale = max(1, int(per_step_budget / max(dt, 1e-6)))
-    sample_envs = min(envs_total, sample_envs * scale)
-    sample_envs = max(threads, (sample_envs // threads) * threads)
+    sample_envs = min(envs_total, threads * 8)
+    while True:
+        sim, env = make(sample_envs, 0)
+        sim.step(wl.actions(env, 0))
+        t0 = time.perf_counter()
+        sim.step(wl.actions(env, 1))
+        dt = time.perf_counter() - t0
+        if sample_envs >= envs_total or dt >= 0.7 * per_step_budget:
+            break
+        grow = max(2.0, min(16.0, per_step_budget / max(dt, 1e-6)))
+        sample_envs = min(envs_total, max(threads, int(sample_envs * grow) // threads * threads))
     sim, env = make(sample_envs, 0)
     for s in range(warmup):
         sim.step(wl.actions(env, s))
