@@ -228,6 +228,27 @@ def profile_traffic() -> float | None:
     return None
 
 
+def shard(rank: int, envs_per_rank: int) -> tuple[int, np.ndarray]:
+    """Global env range of one rank: [rank * n, (rank + 1) * n)."""
+    offset = rank * envs_per_rank
+    return offset, np.arange(offset, offset + envs_per_rank)
+
+
+def combine_over_ranks(elapsed_ms: float, e2e_s: float | None, instr: int, device, world: int):
+    """Max over ranks of the device and end-to-end times, sum of emulated instructions."""
+    import torch
+    import torch.distributed as dist
+
+    if world <= 1:
+        return elapsed_ms, e2e_s, instr
+    vals = torch.tensor([elapsed_ms, e2e_s or 0.0, float(instr)], dtype=torch.float64, device=device)
+    mx = vals.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    sm = vals.clone()
+    dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    return float(mx[0]), (float(mx[1]) if e2e_s is not None else None), int(sm[2])
+
+
 def run_ours(args, rank, world, local) -> dict | None:
     import torch
     import torch.distributed as dist
@@ -244,8 +265,7 @@ def run_ours(args, rank, world, local) -> dict | None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     wl = make_workload(args.workload)
     n = args.envs
-    offset = rank * n
-    env = np.arange(offset, offset + n)
+    offset, env = shard(rank, n)
     e2l = wl.env_to_level(env) if wl.env_to_level else None
     batch = CudaBatch(n, wl.frameskip, wl.rom.image, wl.snapshots if wl.snapshots else None,
                       e2l if len(wl.snapshots) > 1 else None, device=local, done_mode=wl.done_mode,
@@ -295,14 +315,7 @@ def run_ours(args, rank, world, local) -> dict | None:
         assert out["rewards"].shape == (n,)
         barrier()
 
-    vals = torch.tensor([elapsed_ms, e2e_s or 0.0, float(instr)], dtype=torch.float64, device=dev)
-    if world > 1:
-        mx = vals.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = vals.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        elapsed_ms, e2e_s = float(mx[0]), float(mx[1])
-        instr = int(sm[2])
+    elapsed_ms, e2e_s, instr = combine_over_ranks(elapsed_ms, e2e_s, instr, dev, world)
     clock_summary = clocks.summary()
 
     result = None
