@@ -392,6 +392,208 @@ def random_loop_rom(seed: int, *, blocks: int = 256, per_block: int = 16,
     return RomInfo(ines_image(bytes(prg), chr_rom), LOOP_HEAD, NMI_HANDLER, loop_bytes)
 
 
+# Zero-page cells of the sprite/scroll ROM.  Random stores may overwrite them;
+# that only perturbs the RNG, the scroll or the frame handshake, never control flow.
+ZP_RNG, ZP_JOY, ZP_SCROLL, ZP_NMI_FLAG, ZP_PTR = 0xF0, 0xF1, 0xF2, 0xF3, 0xF4
+NT_IMAGE = 0xE000       # 2 KB nametable image (both physical nametables) copied at reset
+PALETTE_IMAGE = 0xE800  # 32 palette bytes
+OPAQUE_TILE = 0xFF      # all-opaque tile in both pattern tables
+SPRITE0_Y = 30
+SPRITE_LOOP_HEAD = 0x8100  # the reset code is longer than the 16 bytes below LOOP_HEAD
+
+
+def _lcg_byte(a: Asm) -> None:
+    """A = rng = rng * 5 + $1B (mod 256): full period, no fixed point."""
+    a.emit("LDA", ZP, ZP_RNG)
+    a.emit("ASL", ACC)
+    a.emit("ASL", ACC)
+    a.emit("CLC")
+    a.emit("ADC", ZP, ZP_RNG)
+    a.emit("CLC")
+    a.emit("ADC", IMM, 0x1B)
+    a.emit("STA", ZP, ZP_RNG)
+
+
+def sprite_scroll_rom(seed: int, *, blocks: int = 8, per_block: int = 16) -> RomInfo:
+    """Sprite- and scroll-heavy mapper-0 image (the pixel-mode configuration).
+
+    Reset copies a 2 KB nametable image (random tiles and attributes, rows 3-4
+    of both nametables the all-opaque tile $FF) and a random palette through
+    $2006/$2007, then enables rendering and NMI ($2001=$1E, $2000=$80).
+
+    Main loop, once per frame: strobe the controller and fold its 8 bits into
+    an 8-bit LCG; fill sprites 1-63 of the OAM buffer at $0200 with LCG bytes
+    (uniform X, Y, tile, attribute); put sprite 0 at Y=30 on tile $FF (opaque,
+    over the opaque band, so the hit is certain); run ``blocks`` random blocks;
+    wait for the NMI handler's flag.
+
+    NMI handler (saves A, X, Y): OAM DMA from page $02; horizontal scroll +=
+    (joypad & 3) + 1 written to $2005 for the next frame; wait for the
+    sprite-0 flag to clear (pre-render line) and then to set (line 30); write
+    $2005 again with an LCG byte (the mid-frame split); set the flag.
+    """
+    rng = np.random.default_rng(seed)
+    prg = bytearray([FILL_BYTE]) * 32768
+
+    reset = Asm(PRG_BASE)
+    reset.emit("SEI")
+    reset.emit("CLD")
+    reset.emit("LDX", IMM, 0xFF)
+    reset.emit("TXS")
+    reset.emit("LDA", IMM, 0x00)
+    reset.emit("STA", ABS, 0x2000)
+    reset.emit("STA", ABS, 0x2001)
+    reset.emit("LDA", ABS, 0x2002)          # reset the $2005/$2006 latch
+    reset.emit("LDA", IMM, 0x3F)
+    reset.emit("STA", ABS, 0x2006)
+    reset.emit("LDA", IMM, 0x00)
+    reset.emit("STA", ABS, 0x2006)
+    reset.emit("LDX", IMM, 0x00)
+    reset.label("pal")
+    reset.emit("LDA", ABSX, PALETTE_IMAGE)
+    reset.emit("STA", ABS, 0x2007)
+    reset.emit("INX")
+    reset.emit("CPX", IMM, 32)
+    reset.branch("BNE", "pal")
+    reset.emit("LDA", IMM, 0x20)
+    reset.emit("STA", ABS, 0x2006)
+    reset.emit("LDA", IMM, 0x00)
+    reset.emit("STA", ABS, 0x2006)
+    reset.emit("LDA", IMM, NT_IMAGE & 0xFF)
+    reset.emit("STA", ZP, ZP_PTR)
+    reset.emit("LDA", IMM, NT_IMAGE >> 8)
+    reset.emit("STA", ZP, ZP_PTR + 1)
+    reset.emit("LDX", IMM, 8)               # 8 pages of 256 bytes
+    reset.emit("LDY", IMM, 0)
+    reset.label("nt")
+    reset.emit("LDA", INDY, ZP_PTR)
+    reset.emit("STA", ABS, 0x2007)
+    reset.emit("INY")
+    reset.branch("BNE", "nt")
+    reset.emit("INC", ZP, ZP_PTR + 1)
+    reset.emit("DEX")
+    reset.branch("BNE", "nt")
+    reset.emit("LDA", IMM, int(rng.integers(1, 256)))
+    reset.emit("STA", ZP, ZP_RNG)
+    reset.emit("LDA", IMM, 0x00)
+    reset.emit("STA", ZP, ZP_SCROLL)
+    reset.emit("STA", ZP, ZP_NMI_FLAG)
+    reset.emit("STA", ABS, 0x2005)
+    reset.emit("STA", ABS, 0x2005)
+    # Rendering first: enabling NMI inside vblank raises the NMI at once, and
+    # the handler's sprite-0 wait needs rendering on.
+    reset.emit("LDA", IMM, 0x1E)
+    reset.emit("STA", ABS, 0x2001)
+    reset.emit("LDA", IMM, 0x80)
+    reset.emit("STA", ABS, 0x2000)
+    reset.emit("JMP", ABS, SPRITE_LOOP_HEAD)
+    code, _ = reset.assemble()
+    if PRG_BASE + len(code) > SPRITE_LOOP_HEAD:
+        raise ValueError("reset code overlaps the main loop")
+    _place(prg, PRG_BASE, code)
+
+    loop = Asm(SPRITE_LOOP_HEAD)
+    # controller -> joy, rng ^= joy
+    loop.emit("LDA", IMM, 0x01)
+    loop.emit("STA", ABS, 0x4016)
+    loop.emit("LSR", ACC)
+    loop.emit("STA", ABS, 0x4016)
+    loop.emit("LDX", IMM, 8)
+    loop.label("joy")
+    loop.emit("LDA", ABS, 0x4016)
+    loop.emit("LSR", ACC)
+    loop.emit("ROL", ZP, ZP_JOY)
+    loop.emit("DEX")
+    loop.branch("BNE", "joy")
+    loop.emit("LDA", ZP, ZP_JOY)
+    loop.emit("EOR", ZP, ZP_RNG)
+    loop.emit("STA", ZP, ZP_RNG)
+    # sprites 1..63
+    loop.emit("LDX", IMM, 4)
+    loop.label("fill")
+    _lcg_byte(loop)
+    loop.emit("STA", ABSX, 0x0200)
+    loop.emit("INX")
+    loop.branch("BNE", "fill")
+    # sprite 0: Y=30, opaque tile, front priority, X in [$40, $BF]
+    loop.emit("LDA", IMM, SPRITE0_Y)
+    loop.emit("STA", ABS, 0x0200)
+    loop.emit("LDA", IMM, OPAQUE_TILE)
+    loop.emit("STA", ABS, 0x0201)
+    loop.emit("LDA", IMM, 0x00)
+    loop.emit("STA", ABS, 0x0202)
+    _lcg_byte(loop)
+    loop.emit("AND", IMM, 0x7F)
+    loop.emit("CLC")
+    loop.emit("ADC", IMM, 0x40)
+    loop.emit("STA", ABS, 0x0203)
+    for b in range(blocks):
+        emit_random_block(loop, rng, f"s{b}", per_block)
+    loop.label("wait")
+    loop.emit("LDA", ZP, ZP_NMI_FLAG)
+    loop.branch("BEQ", "wait")
+    loop.emit("LDA", IMM, 0x00)
+    loop.emit("STA", ZP, ZP_NMI_FLAG)
+    loop.emit("JMP", ABS, SPRITE_LOOP_HEAD)
+    code, _ = loop.assemble()
+    loop_bytes = len(code)
+    if SPRITE_LOOP_HEAD + len(code) > NT_IMAGE:
+        raise ValueError("main loop does not fit below the nametable image")
+    _place(prg, SPRITE_LOOP_HEAD, code)
+
+    nt = rng.integers(0, 256, size=2048, dtype=np.uint8)
+    for base in (0, 1024):  # both physical nametables: rows 3-4 opaque band
+        nt[base + 3 * 32: base + 5 * 32] = OPAQUE_TILE
+    _place(prg, NT_IMAGE, nt.tobytes())
+    pal = (rng.integers(0, 64, size=32, dtype=np.uint8)).tobytes()
+    _place(prg, PALETTE_IMAGE, pal)
+
+    nmi = Asm(NMI_HANDLER)
+    nmi.emit("PHA")
+    nmi.emit("TXA")
+    nmi.emit("PHA")
+    nmi.emit("TYA")
+    nmi.emit("PHA")
+    nmi.emit("LDA", IMM, 0x02)
+    nmi.emit("STA", ABS, 0x4014)
+    nmi.emit("LDA", ZP, ZP_JOY)
+    nmi.emit("AND", IMM, 0x03)
+    nmi.emit("SEC")
+    nmi.emit("ADC", ZP, ZP_SCROLL)
+    nmi.emit("STA", ZP, ZP_SCROLL)
+    nmi.emit("STA", ABS, 0x2005)
+    nmi.emit("LDA", IMM, 0x00)
+    nmi.emit("STA", ABS, 0x2005)
+    nmi.label("clear")
+    nmi.emit("BIT", ABS, 0x2002)
+    nmi.branch("BVS", "clear")
+    nmi.label("hit")
+    nmi.emit("BIT", ABS, 0x2002)
+    nmi.branch("BVC", "hit")
+    _lcg_byte(nmi)
+    nmi.emit("STA", ABS, 0x2005)
+    nmi.emit("LDA", IMM, 0x00)
+    nmi.emit("STA", ABS, 0x2005)
+    nmi.emit("LDA", IMM, 0x01)
+    nmi.emit("STA", ZP, ZP_NMI_FLAG)
+    nmi.emit("PLA")
+    nmi.emit("TAY")
+    nmi.emit("PLA")
+    nmi.emit("TAX")
+    nmi.emit("PLA")
+    nmi.emit("RTI")
+    code, _ = nmi.assemble()
+    _place(prg, NMI_HANDLER, code)
+    _place(prg, IRQ_STUB, bytes([op("RTI")]))
+    _vectors(prg, NMI_HANDLER, PRG_BASE, IRQ_STUB)
+
+    chr_rom = bytearray(rng.integers(0, 256, size=8192, dtype=np.uint8).tobytes())
+    for table in (0x0000, 0x1000):
+        off = table + OPAQUE_TILE * 16
+        chr_rom[off:off + 16] = b"\xff" * 16
+    return RomInfo(ines_image(bytes(prg), bytes(chr_rom)), SPRITE_LOOP_HEAD, NMI_HANDLER, loop_bytes)
+
+
 # ---------------------------------------------------------------------------
 # FCEUX FCS save states (the snapshot input format of the reference binding,
 # cpp/include/nesle/fcs.hpp:187-226): 16-byte header "FCS\xff", then chunks
@@ -517,4 +719,14 @@ def config4(seed: int = 4) -> Workload:
                     DONE_FRAME_LIMIT, (500, 5000), 4, seed)
 
 
-CONFIGS = {"config1": config1, "config2": config2, "config4": config4}
+def config3(seed: int = 3) -> Workload:
+    """Pixel mode: sprite/scroll ROM from power-on, uniform joypad bytes (they drive
+    the scroll and the sprite RNG), done at a per-episode frame limit in [500, 5000];
+    the observation is the 84x84 gray downsample of the palette-index frame."""
+    rom = sprite_scroll_rom(seed)
+    return Workload("config3-pixel", rom, [], None,
+                    lambda env, step: uniform_actions(seed, env, step),
+                    DONE_FRAME_LIMIT, (500, 5000), 4, seed)
+
+
+CONFIGS = {"config1": config1, "config2": config2, "config3": config3, "config4": config4}

@@ -40,6 +40,7 @@ CASES = [
     ("config1_B", w.config1, "B", 8, 6, False),
     ("config1_A", w.config1, "A", 8, 6, False),
     ("config2_B", w.config2, "B", 8, 6, True),
+    ("config3_B", w.config3, "B", 8, 6, True),
     ("config4_B", w.config4, "B", 8, 6, True),
     ("config4_short_B", None, "B", 8, 12, True),  # frame limit [6, 20]: many auto-resets
 ]

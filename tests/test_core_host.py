@@ -11,9 +11,28 @@ from nesle_b200 import workloads as w
 from oracle import Oracle
 
 
-@pytest.mark.parametrize("make,auto_reset", [(w.config1, False), (w.config2, True), (w.config4, True)])
+@pytest.mark.parametrize("make,auto_reset", [(w.config1, False), (w.config2, True), (w.config3, True),
+                                             (w.config4, True)])
 def test_configs_lockstep(make, auto_reset):
     run_lockstep(make, 8, 8, auto_reset, [HostCore, HostCoreGlobal])
+
+
+def test_config3_frames_match_checker_every_step():
+    """Pixel mode: index, RGB and 84x84 gray frames after every env-step."""
+    wl = w.config3()
+    n = 4
+    env = np.arange(n)
+    kw = dict(done_mode=wl.done_mode, done_args=wl.done_args, seed=wl.seed)
+    o = Oracle(n, 4, wl.rom.image, [], **kw)
+    h = HostCoreGlobal(n, 4, wl.rom.image, [], **kw)
+    for s in range(4):
+        a = wl.actions(env, s)
+        o.step(a)
+        h.step(a)
+        ro, rh = o.render(), h.render()
+        for k in ("index", "rgb", "gray84"):
+            np.testing.assert_array_equal(ro[k], rh[k], err_msg=f"step {s} {k}")
+    assert all(len(np.unique(ro["index"][e])) > 4 for e in range(n))
 
 
 def test_frame_limit_auto_reset_lockstep():

@@ -25,7 +25,8 @@ def _short_config4() -> w.Workload:
     return wl
 
 
-MAKERS = {"config1": w.config1, "config2": w.config2, "config4": w.config4, "config4_short": _short_config4}
+MAKERS = {"config1": w.config1, "config2": w.config2, "config3": w.config3, "config4": w.config4,
+          "config4_short": _short_config4}
 
 
 def _cases() -> list[str]:
@@ -64,7 +65,7 @@ def _replay(case: str, make_sim) -> None:
 
 
 def test_fixture_covers_every_benchmark_config():
-    assert {c.rsplit("_", 1)[0] for c in _cases()} >= {"config1", "config2", "config4"}
+    assert {c.rsplit("_", 1)[0] for c in _cases()} >= {"config1", "config2", "config3", "config4"}
     assert "config1_A" in _cases()  # the reference CPU core, not only the batched semantics
 
 

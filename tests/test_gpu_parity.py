@@ -28,7 +28,7 @@ def _cuda():
 
 
 @pytest.mark.parametrize("make,auto_reset,n", [(w.config1, False, 64), (w.config2, True, 200),
-                                               (w.config4, True, 200)])
+                                               (w.config3, True, 200), (w.config4, True, 200)])
 @pytest.mark.parametrize("variant", ["shared", "global"])
 def test_configs_lockstep(make, auto_reset, n, variant, monkeypatch):
     """Every step, every field, against the checker (200 envs = 2 full CTAs + a partial one),
@@ -106,6 +106,24 @@ def test_render_index_rgb_gray_match_checker():
     for k in ("index", "rgb", "gray84"):
         np.testing.assert_array_equal(ro[k], rg[k], err_msg=k)
     assert len(np.unique(ro["index"])) > 8
+
+
+def test_config3_frames_every_step():
+    """Pixel mode on the GPU: index, RGB and 84x84 gray frames after every env-step."""
+    wl = w.config3()
+    n = 64
+    env = np.arange(n)
+    kw = dict(done_mode=wl.done_mode, done_args=wl.done_args, seed=wl.seed)
+    o = Oracle(n, 4, wl.rom.image, [], **kw)
+    g = GpuCore(n, 4, wl.rom.image, [], **kw)
+    for s in range(4):
+        a = wl.actions(env, s)
+        o.step(a)
+        g.step(a)
+        assert_same(o, g)
+        ro, rg = o.render(), g.render()
+        for k in ("index", "rgb", "gray84"):
+            np.testing.assert_array_equal(ro[k], rg[k], err_msg=f"step {s} {k}")
 
 
 def test_reset_envs_poke_and_host_step():
