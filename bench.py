@@ -42,8 +42,11 @@ UNIT = "env-steps/s"
 # Algorithmic HBM bytes of one env-step in RAM mode: one compulsory round trip
 # of the mutable per-env state (2 KB RAM read + write, OAM 256 written, CPU and
 # PPU scalars 88, controller/DMA/reward baselines 30, action 1, reward 4 +
-# done 1) -- see DESIGN.md "Roofline".
+# done 1).
 BYTES_PER_ENV_STEP = 4476
+# Pixel mode adds the observation pass: presentation nametables 2048, palette 32
+# and OAM 256 read, the 84x84 observation 7056 written (13,868 B/env-step in all).
+BYTES_PER_OBS = 2048 + 32 + 256 + 7056
 
 
 def parse_args(argv=None):
@@ -53,7 +56,7 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--envs", type=int, default=65536, help="envs per GPU")
-    ap.add_argument("--workload", default="config4", choices=["config4", "config2", "config1"])
+    ap.add_argument("--workload", default="config4", choices=["config4", "config3", "config2", "config1"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args(argv)
@@ -69,16 +72,21 @@ def dist_env():
 def make_workload(name: str):
     from nesle_b200 import workloads as w
 
-    return {"config4": w.config4, "config2": w.config2, "config1": w.config1}[name]()
+    return {"config4": w.config4, "config3": w.config3, "config2": w.config2, "config1": w.config1}[name]()
+
+
+def is_pixel(wl) -> bool:
+    return wl.name.startswith("config3")
 
 
 def workload_config(wl, envs: int, world: int) -> dict:
     return {
-        "workload": f"{wl.name}: BASELINE config {wl.name[6]}" if wl.name.startswith("config") else wl.name,
+        "workload": f"{wl.name}: benchmark config {wl.name[6]}" if wl.name.startswith("config") else wl.name,
         "envs_per_gpu": envs,
         "total_envs": envs * world,
         "frameskip": wl.frameskip,
-        "observation": "ram (2048 B/env, zero-copy view)",
+        "observation": ("gray 84x84 (7056 B/env) rendered every env-step from the palette-index frame"
+                        if is_pixel(wl) else "ram (2048 B/env, zero-copy view)"),
         "snapshots": len(wl.snapshots),
         "done": {0: "smb", 1: "RAM[$FF]==$FF", 2: "frame limit U[500,5000]"}[wl.done_mode],
         "auto_reset": "fused",
@@ -214,9 +222,9 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "_fallback": True}
 
 
-def profile_traffic() -> float | None:
-    """DRAM bytes per launch of the step kernel from the committed ncu summary."""
-    p = ROOT / "profiles" / "step_kernel_config4.txt"
+def profile_traffic(summary: str = "step_kernel_config4.txt") -> float | None:
+    """DRAM bytes per launch of a kernel from its committed ncu summary."""
+    p = ROOT / "profiles" / summary
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -278,23 +286,35 @@ def run_ours(args, rank, world, local) -> dict | None:
         if world > 1:
             dist.barrier(device_ids=[local])
 
-    for s in range(args.warmup):
+    pixel = is_pixel(wl)
+
+    def device_step(s):
         batch.step_device(acts[s], auto_reset=True, synchronize=False)
+
+    for s in range(args.warmup):
+        device_step(s)
+        if pixel:
+            batch.obs_gray84_device(render=True)
     torch.cuda.synchronize(dev)
     barrier()
     torch.cuda.synchronize(dev)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     instr = 0
     with ClockSampler(local) as clocks:
         time.sleep(0.3)  # let the sampler attach
         for i, s in enumerate(range(args.warmup, total_steps)):
             starts[i].record(stream)
-            batch.step_device(acts[s], auto_reset=True, synchronize=False)
+            device_step(s)
+            mids[i].record(stream)
+            if pixel:
+                batch.obs_gray84_device(render=True)  # the observation of this env-step
             ends[i].record(stream)
         torch.cuda.synchronize(dev)
     barrier()
-    per_step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    per_step_ms = [a.elapsed_time(b) for a, b in zip(starts, mids)]
+    per_obs_ms = [a.elapsed_time(b) for a, b in zip(mids, ends)]
     elapsed_ms = starts[0].elapsed_time(ends[-1])
     instr = int(batch.get_field("stat_instructions").astype(np.int64).sum())  # last step only
     batch.synchronize()  # raises on illegal-opcode faults
@@ -305,12 +325,14 @@ def run_ours(args, rank, world, local) -> dict | None:
         host_acts = torch.empty((total_steps, n), dtype=torch.uint8, pin_memory=True)
         host_acts.copy_(acts.cpu())
         host_np = host_acts.numpy()
+        obs_kw = dict(render_frame=False, copy_obs=True, obs_mode="gray84") if pixel else \
+            dict(render_frame=False, copy_obs=False)
         for s in range(args.warmup):
-            batch.step(host_np[s], render_frame=False, copy_obs=False)
+            batch.step(host_np[s], **obs_kw)
         barrier()
         t0 = time.perf_counter()
         for s in range(args.warmup, total_steps):
-            out = batch.step(host_np[s], render_frame=False, copy_obs=False)
+            out = batch.step(host_np[s], **obs_kw)
         e2e_s = time.perf_counter() - t0
         assert out["rewards"].shape == (n,)
         barrier()
@@ -323,30 +345,43 @@ def run_ours(args, rank, world, local) -> dict | None:
         total_env_steps = n * world * args.steps
         value = total_env_steps / (elapsed_ms / 1e3)
         kernel_ms = statistics.mean(per_step_ms)
+        obs_ms = statistics.mean(per_obs_ms) if pixel else 0.0
         peaks = measured_peaks()
         peak = float(peaks.get("hbm_gbs", 6650.0))
-        achieved = BYTES_PER_ENV_STEP * n / (kernel_ms / 1e3) / 1e9
-        traffic = profile_traffic()
         sm_mhz = clock_summary.get("sm_mhz") or float(peaks.get("sm_max_mhz", 1965.0))
+        step_roof = {"kernel": "step_kernel_global", "bound": "hbm",
+                     "achieved": BYTES_PER_ENV_STEP * n / (kernel_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "traffic": profile_traffic(), "ms": kernel_ms,
+                     "note": "of measured HBM copy bandwidth; the kernel is latency/issue-bound (see issue)"}
+        step_roof["frac"] = step_roof["achieved"] / peak
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
             "config": workload_config(wl, n, world),
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "note": "of measured HBM copy bandwidth; the kernel is issue-bound (see issue)"},
+            "roofline": step_roof,
             "issue": {"emulated_instructions_per_s": instr / (kernel_ms / 1e3) if instr else None,
                       "emulated_instructions_per_env_step": instr / (n * world) if instr else None,
                       "peak_warp_issue_per_s": 148 * 4 * sm_mhz * 1e6},
             "kernel_ms": kernel_ms,
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * (2 if pixel else 1),
             "clocks": clock_summary,
         }
+        if pixel:
+            obs_roof = {"kernel": "gray84_kernel", "bound": "hbm",
+                        "achieved": BYTES_PER_OBS * n / (obs_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                        "traffic": profile_traffic("gray84_kernel_config3.txt"), "ms": obs_ms}
+            obs_roof["frac"] = obs_roof["achieved"] / peak
+            result["obs_kernel"] = obs_roof
+            if obs_ms > kernel_ms:  # the roofline object describes the dominant kernel
+                result["roofline"], result["obs_kernel"] = obs_roof, step_roof
         if e2e_s:
+            d2h = (5 + (84 * 84 if pixel else 0)) * n * world
             result["e2e"] = {"value": total_env_steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": n * world,
-                             "d2h_bytes_per_step": 5 * n * world,
-                             "path": "CudaBatch.step(pinned u8 actions) -> rewards, dones as numpy"}
+                             "d2h_bytes_per_step": d2h,
+                             "path": ("CudaBatch.step(pinned u8 actions, obs_mode='gray84') -> obs, rewards, dones "
+                                      "as numpy" if pixel else
+                                      "CudaBatch.step(pinned u8 actions) -> rewards, dones as numpy")}
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = reference_cpu_rate(wl, n, steps=2, warmup=1)
     if world > 1:

@@ -187,9 +187,18 @@ class CudaBatch:
             self._ptr_cache[which] = (int(p.value), int(nb.value))
         return self._ptr_cache[which]
 
-    def _field(self, name: str) -> np.ndarray:
+    def _field(self, name: str, pinned: bool = False) -> np.ndarray:
+        """Host copy of a per-env field.  ``pinned`` (large frame copies) lands it
+        in page-locked memory from torch's caching host allocator, which the
+        DMA engine fills at full speed; the array is still a fresh one."""
         dtype, shape = _lib.FIELDS[name]
-        out = np.empty((self.num_envs, *shape), dtype=dtype)
+        torch = _torch() if pinned else None
+        if torch is not None and torch.cuda.is_available():
+            nbytes = int(np.prod((self.num_envs, *shape))) * np.dtype(dtype).itemsize
+            out = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True).numpy().view(dtype)
+            out = out.reshape((self.num_envs, *shape))
+        else:
+            out = np.empty((self.num_envs, *shape), dtype=dtype)
         self._check(self._lib.nesle_copy_field(self._h, name.encode(), out.ctypes.data, out.nbytes))
         return out
 
@@ -214,17 +223,28 @@ class CudaBatch:
         self.synchronize()
         return self.ram_device()
 
-    def step(self, actions: Any, render_frame: bool = True, copy_obs: bool = True) -> dict:
-        """Host-array step (cuda_module.cu:533-592): rewards/dones as numpy."""
+    _OBS_MODES = {"rgb": (_lib.RENDER_RGB, "frames_rgb"), "index": (_lib.RENDER_INDEX, "frames_index"),
+                  "gray84": (_lib.RENDER_GRAY84, "obs_gray84")}
+
+    def step(self, actions: Any, render_frame: bool = True, copy_obs: bool = True, obs_mode: str = "rgb") -> dict:
+        """Host-array step (cuda_module.cu:533-592): rewards/dones as numpy.
+
+        ``obs_mode`` (extension): the observation rendered and copied -- "rgb"
+        (N, 240, 256, 3) as in the reference, "index" (N, 240, 256) colour
+        indices, or "gray84" (N, 84, 84) luma.
+        """
+        if obs_mode not in self._OBS_MODES:
+            raise ValueError(f"obs_mode must be one of {sorted(self._OBS_MODES)}")
+        mode, field = self._OBS_MODES[obs_mode]
         a = self._host_actions(actions)
         s = ctypes.c_void_p(self._stream())
         self._check(self._lib.nesle_step(self._h, a.ctypes.data, _lib.ACTIONS_U8, 0, 0, 0, s))
         if render_frame or copy_obs:
-            self._check(self._lib.nesle_render(self._h, _lib.RENDER_RGB, s))
+            self._check(self._lib.nesle_render(self._h, mode, s))
         self.synchronize()
         out = {}
         if copy_obs:
-            out["obs"] = self._copy_frames()
+            out["obs"] = self._field(field, pinned=True)
         out["rewards"] = self._field("rewards")
         out["dones"] = self._field("done")
         return out
@@ -313,7 +333,7 @@ class CudaBatch:
 
     # -- helpers ----------------------------------------------------------
     def _copy_frames(self) -> np.ndarray:
-        return self._field("frames_rgb")
+        return self._field("frames_rgb", pinned=True)
 
     def _device_actions(self, actions: Any) -> tuple[int, int]:
         """(pointer, dtype code) of CUDA actions (cuda_module.cu:259-308)."""

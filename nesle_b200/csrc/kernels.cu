@@ -171,54 +171,125 @@ __global__ void poke_kernel(const BatchView* __restrict__ vp, uint32_t address, 
 }
 
 // --------------------------------------------------------------------------
-// Rendering.  grid.x = env, grid.y = band of 16 rows; 256 threads = 1 column.
+// Rendering, one CTA of kRenderThreads per env.  The env's presentation
+// snapshot (nametables, palette, OAM) and the CHR ROM are staged in shared
+// memory and each scanline's sprites are found once (a 64-bit row mask), so a
+// pixel reads only shared memory and visits only the sprites on its row.
 // --------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
+constexpr uint32_t kRenderThreads = 256;
+constexpr uint32_t kChrMax = 8192;
+
+struct SnapSmem {
+    uint8_t chr[kChrMax];
+    uint8_t nt[kNtBytes];
+    uint8_t pal[kPalBytes];
+    uint8_t oam[kOamBytes];
+    uint8_t res[32];  // resolved palette
+    uint64_t rows[kFrameH];
+    uint64_t cols[kFrameW / 8];
+    uint16_t spat[64 * 16];  // sprite pattern rows, flips applied
+};
+
+__device__ __forceinline__ RenderEnv stage_snapshot(const BatchView& v, uint32_t env, SnapSmem& sm) {
+    const uint32_t tid = threadIdx.x;
+    const uint32_t chr_size = v.chr_size <= kChrMax ? v.chr_size : 0u;
+    for (uint32_t i = tid; i < chr_size / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(sm.chr)[i] = reinterpret_cast<const uint4*>(v.chr)[i];
+    const uint4* nt = reinterpret_cast<const uint4*>(v.snap_nt + (size_t)env * kNtBytes);
+    for (uint32_t i = tid; i < kNtBytes / 16; i += blockDim.x) reinterpret_cast<uint4*>(sm.nt)[i] = nt[i];
+    if (tid < kOamBytes / 16)
+        reinterpret_cast<uint4*>(sm.oam)[tid] = reinterpret_cast<const uint4*>(v.snap_oam + (size_t)env * kOamBytes)[tid];
+    if (tid < kPalBytes / 16)
+        reinterpret_cast<uint4*>(sm.pal)[tid] = reinterpret_cast<const uint4*>(v.snap_pal + (size_t)env * kPalBytes)[tid];
+    __syncthreads();
+    const RenderEnv e = render_env_at(v.rec[env], sm.nt, sm.pal, sm.oam, sm.chr, chr_size, v.horizontal);
+    for (uint32_t y = tid; y < kFrameH; y += blockDim.x) sm.rows[y] = sprite_row_mask(e, y);
+    if (tid < kFrameW / 8) sm.cols[tid] = sprite_col_mask(e, tid);
+    if (tid < 32) sm.res[tid] = (uint8_t)rv_palette(e.lower, tid);
+    const uint32_t h = (e.lower.ctrl & 0x20) ? 16 : 8;
+    for (uint32_t i = tid; i < 64 * 16; i += blockDim.x)
+        if (i % 16 < h) sm.spat[i] = (uint16_t)sprite_pattern_row(e.lower, i / 16, i % 16);
+    __syncthreads();
+    return e;
+}
+
+// Per strip of 20 rows: the background tile entries of each row.
+struct StripSmem {
+    uint32_t tiles[kGrayStripRows][kRowTiles];
+};
+
+// One strip of 20 rows: the tile entries (built by the whole CTA), then one
+// pixel per thread from its row's entries and the sprite tables.
+__device__ __forceinline__ void build_strip(const RenderEnv& e, uint32_t row0, StripSmem& st) {
+    for (uint32_t i = threadIdx.x; i < kGrayStripRows * kRowTiles; i += blockDim.x) {
+        const uint32_t r = i / kRowTiles, j = i % kRowTiles, y = row0 + r;
+        st.tiles[r][j] = slot_entry(bg_view(e, y), y, j);
+    }
+}
+__device__ __forceinline__ uint32_t strip_pixel(const RenderEnv& e, const SnapSmem& sm, const StripSmem& st,
+                                                uint32_t row0, uint32_t x, uint32_t y) {
+    const RenderView& v = bg_view(e, y);
+    const uint32_t bgc = bg_from_entry_tables(v, sm.res, st.tiles[y - row0][tile_slot(v, x)], x, v.sx + x);
+    return compose_pixel_tables(e, sm.res, x, y, bgc, sm.rows[y] & sm.cols[x >> 3], sm.spat);
+}
+
+__global__ void __launch_bounds__(kRenderThreads)
 render_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint32_t rgb) {
+    __shared__ __align__(16) SnapSmem sm;
+    __shared__ StripSmem st;
     const BatchView& v = *vp;
     const uint32_t env = blockIdx.x;
-    const RenderEnv e = render_env(v, v.rec[env], env);
-    const uint32_t x = threadIdx.x;
-    for (uint32_t y = blockIdx.y * 16; y < blockIdx.y * 16 + 16; ++y) {
-        const uint32_t c = render_pixel(e, x, y);
-        const size_t px = (size_t)env * (kFrameW * kFrameH) + y * kFrameW + x;
-        if (rgb) {
-            out[px * 3 + 0] = kPaletteRgb[c * 3 + 0];
-            out[px * 3 + 1] = kPaletteRgb[c * 3 + 1];
-            out[px * 3 + 2] = kPaletteRgb[c * 3 + 2];
-        } else {
-            out[px] = (uint8_t)c;
+    const RenderEnv e = stage_snapshot(v, env, sm);
+    uint8_t* dst = out + (size_t)env * (kFrameW * kFrameH) * (rgb ? 3u : 1u);
+    for (uint32_t row0 = 0; row0 < kFrameH; row0 += kGrayStripRows) {
+        build_strip(e, row0, st);
+        __syncthreads();
+        for (uint32_t p = threadIdx.x; p < kGrayStripRows * kFrameW; p += kRenderThreads) {
+            const uint32_t y = row0 + p / kFrameW, x = p % kFrameW;
+            const uint32_t c = strip_pixel(e, sm, st, row0, x, y);
+            const size_t q = (size_t)y * kFrameW + x;
+            if (rgb) {
+                dst[q * 3 + 0] = kPaletteRgb[c * 3 + 0];
+                dst[q * 3 + 1] = kPaletteRgb[c * 3 + 1];
+                dst[q * 3 + 2] = kPaletteRgb[c * 3 + 2];
+            } else {
+                dst[q] = (uint8_t)c;
+            }
         }
+        __syncthreads();
     }
 }
 
-// 84x84 grey: output (ox, oy) is the integer area average of the luma of the
-// source pixels it covers.  In units of 1/21 px horizontally and 1/7 px
-// vertically, source column sx spans [21 sx, 21 sx + 21) and output column ox
-// [64 ox, 64 ox + 64); source row sy spans [7 sy, 7 sy + 7) and output row oy
-// [20 oy, 20 oy + 20).  Result = (sum(luma * wx * wy) + 640) / 1280.
-__device__ __forceinline__ uint32_t luma_of(uint32_t c) {
-    return (299u * kPaletteRgb[c * 3] + 587u * kPaletteRgb[c * 3 + 1] + 114u * kPaletteRgb[c * 3 + 2] + 500u) / 1000u;
-}
-
-__global__ void __launch_bounds__(128)
+// 84x84 grey observation, one CTA per env, on the same staged snapshot.  The
+// frame is done in 12 strips of 20 source rows: every source pixel is rendered
+// once into a shared luma strip, from which the strip's 7 x 84 outputs are
+// area-summed (gray84_pixel).  Nothing but the 7,056-byte observation is written.
+__global__ void __launch_bounds__(kRenderThreads)
 gray84_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out) {
+    __shared__ __align__(16) SnapSmem sm;
+    __shared__ StripSmem st;
+    __shared__ __align__(16) uint8_t s_luma[kGrayStripRows * kFrameW];
+    __shared__ uint8_t s_lut[64];
     const BatchView& v = *vp;
-    const uint32_t env = blockIdx.x;
-    const RenderEnv e = render_env(v, v.rec[env], env);
-    for (uint32_t o = threadIdx.x; o < kGray * kGray; o += blockDim.x) {
-        const uint32_t oy = o / kGray, ox = o % kGray;
-        const uint32_t y0 = (20 * oy) / 7, y1 = (20 * oy + 19) / 7;
-        const uint32_t x0 = (64 * ox) / 21, x1 = (64 * ox + 63) / 21;
-        uint32_t acc = 0;
-        for (uint32_t sy = y0; sy <= y1; ++sy) {
-            const uint32_t wy = min(7 * sy + 7, 20 * oy + 20) - max(7 * sy, 20 * oy);
-            for (uint32_t sx = x0; sx <= x1; ++sx) {
-                const uint32_t wx = min(21 * sx + 21, 64 * ox + 64) - max(21 * sx, 64 * ox);
-                acc += luma_of(render_pixel(e, sx, sy)) * wx * wy;
-            }
+    const uint32_t env = blockIdx.x, tid = threadIdx.x;
+    if (tid < 64) s_lut[tid] = (uint8_t)luma_of_rgb(kPaletteRgb[tid * 3], kPaletteRgb[tid * 3 + 1], kPaletteRgb[tid * 3 + 2]);
+    const RenderEnv e = stage_snapshot(v, env, sm);  // its barriers also cover s_lut
+
+    uint8_t* dst = out + (size_t)env * kGray * kGray;
+    for (uint32_t k = 0; k < kFrameH / kGrayStripRows; ++k) {
+        const uint32_t row0 = k * kGrayStripRows;
+        build_strip(e, row0, st);
+        __syncthreads();
+        for (uint32_t p = tid; p < kGrayStripRows * kFrameW; p += kRenderThreads) {
+            const uint32_t y = row0 + p / kFrameW, x = p % kFrameW;
+            s_luma[p] = s_lut[strip_pixel(e, sm, st, row0, x, y)];
         }
-        out[(size_t)env * kGray * kGray + o] = (uint8_t)((acc + 640) / 1280);
+        __syncthreads();
+        for (uint32_t o = tid; o < kGrayStripOut * kGray; o += kRenderThreads) {
+            const uint32_t oy = k * kGrayStripOut + o / kGray, ox = o % kGray;
+            dst[oy * kGray + ox] = (uint8_t)gray84_pixel(s_luma, row0, ox, oy);
+        }
+        __syncthreads();
     }
 }
 
@@ -266,9 +337,9 @@ cudaError_t launch_poke(const BatchView* dv, uint32_t num_envs, uint32_t address
 
 cudaError_t launch_render(const BatchView* dv, uint32_t num_envs, uint8_t* out, int mode, cudaStream_t s) {
     if (mode == 2) {
-        gray84_kernel<<<num_envs, 128, 0, s>>>(dv, out);
+        gray84_kernel<<<num_envs, kRenderThreads, 0, s>>>(dv, out);
     } else {
-        render_kernel<<<dim3(num_envs, kFrameH / 16), 256, 0, s>>>(dv, out, mode == 0 ? 1u : 0u);
+        render_kernel<<<num_envs, kRenderThreads, 0, s>>>(dv, out, mode == 0 ? 1u : 0u);
     }
     return cudaGetLastError();
 }

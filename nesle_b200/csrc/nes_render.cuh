@@ -57,21 +57,34 @@ NESLE_HD uint32_t rv_pattern(const RenderView& v, uint32_t tile_base, uint32_t f
     const uint32_t bit = 7 - fx;
     return ((lo >> bit) & 1) | (((hi >> bit) & 1) << 1);
 }
-NESLE_HD uint32_t rv_background(const RenderView& v, uint32_t x, uint32_t y) {  // :161-204
-    if (!(v.mask & 0x08) || (!(v.mask & 0x02) && x < 8)) return 0;
+// Background tile of row y at scrolled column wx (batch_render.cuh:161-204):
+// its pattern row (bits 0-15: low plane, high plane) and palette group (bits
+// 16-17).  Every pixel of the row inside that tile shares the entry.
+NESLE_HD uint32_t rv_tile_entry(const RenderView& v, uint32_t y, uint32_t wx) {
     const uint32_t wy = v.sy + y, cy = (wy % 240) / 8, fy = wy & 7;
     const uint32_t base = v.ctrl & 3;
     const uint32_t nty = ((base >> 1) + wy / 240) & 1;
-    const uint32_t wx = v.sx + x, cx = (wx & 0xFF) / 8, fx = wx & 7;
+    const uint32_t cx = (wx & 0xFF) / 8;
     const uint32_t ntx = ((base & 1) + wx / 256) & 1;
     const uint32_t ntb = 0x2000 + (ntx | (nty << 1)) * 0x400;
     const uint32_t pb = (v.ctrl & 0x10) ? 0x1000 : 0;
     const uint32_t tile = rv_mem(v, ntb + cy * 32 + cx);
-    const uint32_t c = rv_pattern(v, pb + tile * 16, fx, fy);
-    if (c == 0) return 0;
+    const uint32_t lo = rv_mem(v, pb + tile * 16 + fy), hi = rv_mem(v, pb + tile * 16 + fy + 8);
     const uint32_t at = rv_mem(v, ntb + 0x3C0 + (cy / 4) * 8 + cx / 4);
-    const uint32_t shift = ((cy & 2) << 1) | (cx & 2);
-    return rv_palette(v, ((at >> shift) & 3) * 4 + c);
+    const uint32_t group = (at >> (((cy & 2) << 1) | (cx & 2))) & 3;
+    return lo | (hi << 8) | (group << 16);
+}
+// Colour index of background pixel x (scrolled column wx) from its tile entry; 0 = transparent.
+NESLE_HD uint32_t rv_bg_from_entry(const RenderView& v, uint32_t entry, uint32_t x, uint32_t wx) {
+    if (!(v.mask & 0x08) || (!(v.mask & 0x02) && x < 8)) return 0;
+    const uint32_t bit = 7 - (wx & 7);
+    const uint32_t c = ((entry >> bit) & 1) | (((entry >> (8 + bit)) & 1) << 1);
+    if (c == 0) return 0;
+    return rv_palette(v, ((entry >> 16) & 3) * 4 + c);
+}
+NESLE_HD uint32_t rv_background(const RenderView& v, uint32_t x, uint32_t y) {
+    const uint32_t wx = v.sx + x;
+    return rv_bg_from_entry(v, rv_tile_entry(v, y, wx), x, wx);
 }
 NESLE_HD uint32_t rv_sprite_px(const RenderView& v, uint32_t tile, uint32_t attr, uint32_t px, uint32_t py) {  // :206-240
     if (attr & 0x40) px = 7 - px;
@@ -92,15 +105,18 @@ struct RenderEnv {
     int split;
 };
 
-NESLE_HD RenderEnv render_env(const BatchView& bv, const EnvRecord& r, uint32_t env) {
+// The views read the presentation snapshot through the given pointers (global
+// rows, or a CTA's shared-memory copy of them).
+NESLE_HD RenderEnv render_env_at(const EnvRecord& r, const uint8_t* nt, const uint8_t* pal, const uint8_t* oam,
+                                 const uint8_t* chr, uint32_t chr_size, uint32_t horizontal) {
     RenderEnv e;
     RenderView play;
-    play.nt = bv.snap_nt + (size_t)env * kNtBytes;
-    play.pal = bv.snap_pal + (size_t)env * kPalBytes;
-    play.oam = bv.snap_oam + (size_t)env * kOamBytes;
-    play.chr = bv.chr;
-    play.chr_size = bv.chr_size;
-    play.horizontal = bv.horizontal;
+    play.nt = nt;
+    play.pal = pal;
+    play.oam = oam;
+    play.chr = chr;
+    play.chr_size = chr_size;
+    play.horizontal = horizontal;
     play.sx = r.snap_sx_end; play.sy = r.snap_sy_end; play.ctrl = r.snap_ctrl_end; play.mask = r.snap_mask;
     e.hud = play;
     e.hud.sx = r.snap_sx_start; e.hud.sy = r.snap_sy_start; e.hud.ctrl = r.snap_ctrl_start;
@@ -111,22 +127,64 @@ NESLE_HD RenderEnv render_env(const BatchView& bv, const EnvRecord& r, uint32_t 
     return e;
 }
 
-// render_batch_rgb_pixel_env (:378-434), returning the colour index.
-NESLE_HD uint32_t render_pixel(const RenderEnv& e, uint32_t x, uint32_t y) {
-    const RenderView& bg = ((int)y < e.split) ? e.hud : e.lower;
+NESLE_HD RenderEnv render_env(const BatchView& bv, const EnvRecord& r, uint32_t env) {
+    return render_env_at(r, bv.snap_nt + (size_t)env * kNtBytes, bv.snap_pal + (size_t)env * kPalBytes,
+                         bv.snap_oam + (size_t)env * kOamBytes, bv.chr, bv.chr_size, bv.horizontal);
+}
+
+// Bit i set when sprite i covers scanline y (the row test of the sprite loop,
+// hoisted so a pixel visits only the sprites on its row).
+NESLE_HD uint64_t sprite_row_mask(const RenderEnv& e, uint32_t y) {
     const RenderView& s = e.lower;
-    uint32_t c = rv_background(bg, x, y);
-    if (c == 0) c = rv_palette(s, 0);
+    const int h = (s.ctrl & 0x20) ? 16 : 8;
+    uint64_t m = 0;
+    for (uint32_t i = 0; i < 64; ++i) {
+        const int sy = (int)y - ((int)s.oam[i * 4] + 1);
+        if (sy >= 0 && sy < h) m |= 1ull << i;
+    }
+    return m;
+}
+
+// Bit i set when sprite i overlaps pixel columns 8 g .. 8 g + 7 (a sprite
+// covers X .. X + 7); ANDed with the row mask it leaves the sprites a pixel
+// can see.
+NESLE_HD uint64_t sprite_col_mask(const RenderEnv& e, uint32_t g) {
+    uint64_t m = 0;
+    for (uint32_t i = 0; i < 64; ++i) {
+        const uint32_t x = e.lower.oam[i * 4 + 3];
+        if (x <= 8 * g + 7 && x + 7 >= 8 * g) m |= 1ull << i;
+    }
+    return m;
+}
+
+NESLE_HD uint32_t lowest_set(uint64_t m) {
+#if defined(__CUDA_ARCH__)
+    return (uint32_t)(__ffsll((long long)m) - 1);
+#else
+    return (uint32_t)__builtin_ctzll(m);
+#endif
+}
+
+// The view that paints row y's background (two-region split).
+NESLE_HD const RenderView& bg_view(const RenderEnv& e, uint32_t y) { return ((int)y < e.split) ? e.hud : e.lower; }
+
+// render_batch_rgb_pixel_env (:378-434) given the pixel's background colour
+// `bgc` (rv_background of bg_view), returning the colour index; `rows` is the
+// sprite_row_mask of scanline y (lowest index still wins).
+NESLE_HD uint32_t compose_pixel(const RenderEnv& e, uint32_t x, uint32_t y, uint32_t bgc, uint64_t rows) {
+    const RenderView& s = e.lower;
+    const bool lower_bg = (int)y >= e.split;
+    uint32_t c = bgc ? bgc : rv_palette(s, 0);
     if ((s.mask & 0x10) && ((s.mask & 0x04) || x >= 8)) {
-        const uint32_t h = (s.ctrl & 0x20) ? 16 : 8;
-        for (uint32_t i = 0; i < 64; ++i) {
+        while (rows) {
+            const uint32_t i = lowest_set(rows);
+            rows &= rows - 1;
             const uint8_t* so = s.oam + i * 4;
             const int sy = (int)y - ((int)so[0] + 1);
-            if (sy < 0 || sy >= (int)h) continue;
             const int sx = (int)x - (int)so[3];
             if (sx < 0 || sx >= 8) continue;
             const uint32_t attr = so[2];
-            if ((attr & 0x20) && rv_background(s, x, y) != 0) continue;
+            if ((attr & 0x20) && (lower_bg ? bgc : rv_background(s, x, y)) != 0) continue;
             const uint32_t sc = rv_sprite_px(s, so[1], attr, (uint32_t)sx, (uint32_t)sy);
             if (sc == 0) continue;
             c = rv_palette(s, 0x10 + (attr & 3) * 4 + sc);
@@ -134,6 +192,107 @@ NESLE_HD uint32_t render_pixel(const RenderEnv& e, uint32_t x, uint32_t y) {
         }
     }
     return c;
+}
+
+NESLE_HD uint32_t render_pixel_masked(const RenderEnv& e, uint32_t x, uint32_t y, uint64_t rows) {
+    return compose_pixel(e, x, y, rv_background(bg_view(e, y), x, y), rows);
+}
+
+NESLE_HD uint32_t render_pixel(const RenderEnv& e, uint32_t x, uint32_t y) {
+    return render_pixel_masked(e, x, y, sprite_row_mask(e, y));
+}
+
+// ---------------------------------------------------------------------------
+// Table-driven form of compose_pixel for the kernels (same result): the env's
+// 32 palette entries resolved once (`res[i]` = rv_palette(view, i); both views
+// share palette and mask), and one entry per sprite covering row y.
+// ---------------------------------------------------------------------------
+NESLE_HD void resolve_palette(const RenderEnv& e, uint8_t* res) {
+    for (uint32_t i = 0; i < 32; ++i) res[i] = (uint8_t)rv_palette(e.lower, i);
+}
+
+// Row r (0..15) of sprite i with any flips applied: pixel sx of the row at
+// bit sx of the low (bits 0-7) and high (bits 8-15) plane.
+NESLE_HD uint32_t sprite_pattern_row(const RenderView& s, uint32_t i, uint32_t r) {
+    const uint8_t* so = s.oam + i * 4;
+    uint32_t lo = 0, hi = 0;
+    for (uint32_t sx = 0; sx < 8; ++sx) {
+        const uint32_t c = rv_sprite_px(s, so[1], so[2], sx, r);
+        lo |= (c & 1u) << sx;
+        hi |= (c >> 1) << sx;
+    }
+    return lo | (hi << 8);
+}
+
+// compose_pixel from the tables; `spat[i * 16 + r]` is sprite_pattern_row(lower, i, r)
+// and `rows` any superset of the sprites covering pixel (x, y) (e.g. the row
+// mask ANDed with the column mask).
+NESLE_HD uint32_t compose_pixel_tables(const RenderEnv& e, const uint8_t* res, uint32_t x, uint32_t y, uint32_t bgc,
+                                       uint64_t rows, const uint16_t* spat) {
+    const RenderView& s = e.lower;
+    uint32_t c = bgc ? bgc : res[0];
+    if ((s.mask & 0x10) && ((s.mask & 0x04) || x >= 8)) {
+        while (rows) {
+            const uint32_t i = lowest_set(rows);
+            rows &= rows - 1;
+            const uint8_t* so = s.oam + i * 4;
+            const uint32_t sx = x - so[3];
+            if (sx >= 8) continue;
+            const uint32_t pat = spat[i * 16 + (y - so[0] - 1)];
+            const uint32_t sc = ((pat >> sx) & 1u) | (((pat >> (8 + sx)) & 1u) << 1);
+            if (sc == 0) continue;
+            const uint32_t attr = so[2];
+            if ((attr & 0x20) && ((int)y >= e.split ? bgc : rv_background(s, x, y)) != 0) continue;
+            c = res[0x10 + (attr & 3) * 4 + sc];
+            break;
+        }
+    }
+    return c;
+}
+
+// Background colour of pixel x from its tile entry and the resolved palette.
+NESLE_HD uint32_t bg_from_entry_tables(const RenderView& v, const uint8_t* res, uint32_t entry, uint32_t x, uint32_t wx) {
+    if (!(v.mask & 0x08) || (!(v.mask & 0x02) && x < 8)) return 0;
+    const uint32_t bit = 7 - (wx & 7);
+    const uint32_t c = ((entry >> bit) & 1) | (((entry >> (8 + bit)) & 1) << 1);
+    return c ? res[((entry >> 16) & 3) * 4 + c] : 0u;
+}
+
+// Tile slots of one row: slot j holds the tile of scrolled column
+// (sx & ~7) + 8 j; 256 pixels touch at most 33 of them.
+constexpr uint32_t kRowTiles = 33;
+NESLE_HD uint32_t tile_slot(const RenderView& v, uint32_t x) { return ((v.sx + x) >> 3) - (v.sx >> 3); }
+NESLE_HD uint32_t slot_entry(const RenderView& v, uint32_t y, uint32_t j) {
+    return rv_tile_entry(v, y, (v.sx & ~7u) + 8 * j);
+}
+
+// 84x84 grey: output (ox, oy) is the integer area average of the luma of the
+// source pixels it covers.  In units of 1/21 px horizontally and 1/7 px
+// vertically, source column sx spans [21 sx, 21 sx + 21) and output column ox
+// [64 ox, 64 ox + 64); source row sy spans [7 sy, 7 sy + 7) and output row oy
+// [20 oy, 20 oy + 20).  Result = (sum(luma * wx * wy) + 640) / 1280.  Source
+// rows [20 k, 20 k + 20) map exactly onto output rows [7 k, 7 k + 7).
+constexpr uint32_t kGrayStripRows = 20, kGrayStripOut = 7;
+
+NESLE_HD uint32_t umin(uint32_t a, uint32_t b) { return a < b ? a : b; }
+NESLE_HD uint32_t umax(uint32_t a, uint32_t b) { return a > b ? a : b; }
+
+NESLE_HD uint32_t luma_of_rgb(uint32_t r, uint32_t g, uint32_t b) {  // BT.601, rounded
+    return (299u * r + 587u * g + 114u * b + 500u) / 1000u;
+}
+
+// One output pixel from a strip of source luma (`luma[row * 256 + x]`, rows
+// relative to `row0`).
+NESLE_HD uint32_t gray84_pixel(const uint8_t* luma, uint32_t row0, uint32_t ox, uint32_t oy) {
+    uint32_t acc = 0;
+    for (uint32_t sy = (20 * oy) / 7; sy <= (20 * oy + 19) / 7; ++sy) {
+        const uint32_t wy = umin(7 * sy + 7, 20 * oy + 20) - umax(7 * sy, 20 * oy);
+        for (uint32_t sx = (64 * ox) / 21; sx <= (64 * ox + 63) / 21; ++sx) {
+            const uint32_t wx = umin(21 * sx + 21, 64 * ox + 64) - umax(21 * sx, 64 * ox);
+            acc += luma[(sy - row0) * kFrameW + sx] * wx * wy;
+        }
+    }
+    return (acc + 640) / 1280;
 }
 
 }  // namespace nesle

@@ -178,31 +178,40 @@ void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) 
 // mode: 0 rgb (N*240*256*3), 1 index (N*240*256), 2 gray84 (N*84*84)
 void host_render(void* p, int mode, uint8_t* out) {
     auto* h = static_cast<HostBatch*>(p);
-    std::vector<uint8_t> fb(kFrameW * kFrameH);
+    std::vector<uint8_t> fb(kFrameW * kFrameH), luma(kFrameW * kFrameH);
     for (uint32_t e = 0; e < h->v.num_envs; ++e) {
         const RenderEnv re = render_env(h->v, h->rec[e], e);
-        for (uint32_t y = 0; y < kFrameH; ++y)
-            for (uint32_t x = 0; x < kFrameW; ++x) fb[y * kFrameW + x] = (uint8_t)render_pixel(re, x, y);
+        uint8_t res[32];
+        resolve_palette(re, res);
+        uint16_t spat[64 * 16] = {};
+        const uint32_t h = (re.lower.ctrl & 0x20) ? 16 : 8;
+        for (uint32_t i = 0; i < 64 * 16; ++i)
+            if (i % 16 < h) spat[i] = (uint16_t)sprite_pattern_row(re.lower, i / 16, i % 16);
+        uint64_t cols[kFrameW / 8];
+        for (uint32_t g = 0; g < kFrameW / 8; ++g) cols[g] = sprite_col_mask(re, g);
+        for (uint32_t y = 0; y < kFrameH; ++y) {  // the kernels' path: row tiles, sprite tables, resolved palette
+            const uint64_t rows = sprite_row_mask(re, y);
+            const RenderView& v = bg_view(re, y);
+            uint32_t tiles[kRowTiles];
+            for (uint32_t j = 0; j < kRowTiles; ++j) tiles[j] = slot_entry(v, y, j);
+            for (uint32_t x = 0; x < kFrameW; ++x) {
+                const uint32_t bgc = bg_from_entry_tables(v, res, tiles[tile_slot(v, x)], x, v.sx + x);
+                fb[y * kFrameW + x] = (uint8_t)compose_pixel_tables(re, res, x, y, bgc, rows & cols[x >> 3], spat);
+            }
+        }
         if (mode == 1) {
             memcpy(out + (size_t)e * fb.size(), fb.data(), fb.size());
         } else if (mode == 0) {
             for (size_t i = 0; i < fb.size(); ++i)
                 for (int ch = 0; ch < 3; ++ch) out[((size_t)e * fb.size() + i) * 3 + ch] = kRgb[fb[i] * 3 + ch];
         } else {
-            for (uint32_t oy = 0; oy < kGray; ++oy)
-                for (uint32_t ox = 0; ox < kGray; ++ox) {
-                    uint32_t acc = 0;
-                    for (uint32_t sy = (20 * oy) / 7; sy <= (20 * oy + 19) / 7; ++sy) {
-                        const uint32_t wy = std::min(7 * sy + 7, 20 * oy + 20) - std::max(7 * sy, 20 * oy);
-                        for (uint32_t sx = (64 * ox) / 21; sx <= (64 * ox + 63) / 21; ++sx) {
-                            const uint32_t wx = std::min(21 * sx + 21, 64 * ox + 64) - std::max(21 * sx, 64 * ox);
-                            const uint32_t c = fb[sy * kFrameW + sx];
-                            const uint32_t l = (299u * kRgb[c * 3] + 587u * kRgb[c * 3 + 1] + 114u * kRgb[c * 3 + 2] + 500u) / 1000u;
-                            acc += l * wx * wy;
-                        }
-                    }
-                    out[(size_t)e * kGray * kGray + oy * kGray + ox] = (uint8_t)((acc + 640) / 1280);
-                }
+            for (size_t i = 0; i < fb.size(); ++i)
+                luma[i] = (uint8_t)luma_of_rgb(kRgb[fb[i] * 3], kRgb[fb[i] * 3 + 1], kRgb[fb[i] * 3 + 2]);
+            for (uint32_t k = 0; k < kFrameH / kGrayStripRows; ++k)
+                for (uint32_t oy = k * kGrayStripOut; oy < (k + 1) * kGrayStripOut; ++oy)
+                    for (uint32_t ox = 0; ox < kGray; ++ox)
+                        out[(size_t)e * kGray * kGray + oy * kGray + ox] =
+                            (uint8_t)gray84_pixel(luma.data() + k * kGrayStripRows * kFrameW, k * kGrayStripRows, ox, oy);
         }
     }
 }
