@@ -82,6 +82,15 @@ int nesle_reset_envs(nesle_batch* b, const uint8_t* mask, int mask_on_device, vo
 int nesle_step(nesle_batch* b, const void* actions, int action_dtype, int actions_on_device,
                int device_api, int auto_reset, void* stream);
 
+/* Replaces CudaBatch.step_profile(actions) (cuda_module.cu:734-818): a
+ * step() (no last_* copy, no auto-reset) that also counts every executed
+ * instruction by opcode and by the address it was fetched from, as
+ * console_step_kernel does (kernels.cu:59-64).  The histograms are cleared
+ * first, then copied to opcode_counts[256] and pc_counts[65536] (host memory;
+ * either may be NULL).  Synchronous. */
+int nesle_step_profile(nesle_batch* b, const void* actions, int action_dtype, int actions_on_device, void* stream,
+                       uint64_t* opcode_counts, uint64_t* pc_counts);
+
 #define NESLE_RENDER_RGB 0    /* (N,240,256,3) uint8, as launch_render_kernel (kernels.cu:160-174) */
 #define NESLE_RENDER_INDEX 1  /* (N,240,256) NES colour indices; no counterpart in the reference */
 #define NESLE_RENDER_GRAY84 2 /* (N,84,84) area-resampled luma; no counterpart in the reference */

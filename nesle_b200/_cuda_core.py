@@ -266,6 +266,19 @@ class CudaBatch:
         out["budget_hits"] = self._field("stat_budget_hits")
         return out
 
+    def step_profile(self, actions: Any) -> dict:
+        """step_stats() plus the instruction histograms of the step (cuda_module.cu:734-818):
+        ``opcode_counts`` (256,) and ``pc_counts`` (65536,) uint64."""
+        a = self._host_actions(actions)
+        ops = np.zeros(256, np.uint64)
+        pcs = np.zeros(65536, np.uint64)
+        self._check(self._lib.nesle_step_profile(self._h, a.ctypes.data, _lib.ACTIONS_U8, 0,
+                                                 ctypes.c_void_p(self._stream()), ops.ctypes.data, pcs.ctypes.data))
+        self._raise_on_fault()
+        return {"rewards": self._field("rewards"), "dones": self._field("done"),
+                "instructions": self._field("stat_instructions"), "frames_completed": self._field("stat_frames"),
+                "budget_hits": self._field("stat_budget_hits"), "opcode_counts": ops, "pc_counts": pcs}
+
     def render(self) -> np.ndarray:
         self.render_device()
         self.synchronize()

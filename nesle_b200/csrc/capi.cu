@@ -59,6 +59,7 @@ struct nesle_batch {
     uint8_t* d_frames_rgb = nullptr;
     uint8_t* d_frames_index = nullptr;
     uint8_t* d_gray84 = nullptr;
+    unsigned long long* d_prof = nullptr;  // step_profile histograms: 256 opcode + 65536 PC counts
     cudaEvent_t done_event = nullptr;
     uint32_t step_variant = kStepGlobalRam;
     uint32_t step_threads = 0;
@@ -311,13 +312,12 @@ int nesle_reset_envs(nesle_batch* b, const uint8_t* mask, int mask_on_device, vo
     return finish(b, s, launch_reset(b->dv, b->n, dmask, false, s), "reset_envs kernel");
 }
 
-int nesle_step(nesle_batch* b, const void* actions, int dtype, int on_device, int device_api, int auto_reset,
-               void* stream) {
+// Shared by nesle_step and nesle_step_profile: action ingest (cuda_module.cu:259-317) and the launch.
+static int step_impl(nesle_batch* b, const void* actions, int dtype, int on_device, int device_api, int auto_reset,
+                     cudaStream_t s, unsigned long long* prof_op, unsigned long long* prof_pc) {
     if (!b || !actions) return fail(NESLE_ERR_INVALID, "step: null argument");
     if (dtype != NESLE_ACTIONS_U8 && dtype != NESLE_ACTIONS_I64)
         return fail(NESLE_ERR_INVALID, "CUDA actions must be uint8 masks or int64 values already encoded as masks");
-    DeviceGuard guard(b->device);
-    auto s = static_cast<cudaStream_t>(stream);
     const uint8_t* a8 = nullptr;
     const long long* a64 = nullptr;
     if (on_device) {
@@ -329,7 +329,34 @@ int nesle_step(nesle_batch* b, const void* actions, int dtype, int on_device, in
         a8 = b->d_host_actions;
     }
     uint32_t flags = (device_api ? kStepDeviceApi : 0u) | (auto_reset ? kStepAutoReset : 0u);
-    return finish(b, s, launch_step(b->dv, b->n, a8, a64, flags, b->step_variant, b->step_threads, s), "step kernel");
+    return finish(b, s, launch_step(b->dv, b->n, a8, a64, flags, b->step_variant, b->step_threads, s, prof_op, prof_pc),
+                  "step kernel");
+}
+
+int nesle_step(nesle_batch* b, const void* actions, int dtype, int on_device, int device_api, int auto_reset,
+               void* stream) {
+    if (!b) return fail(NESLE_ERR_INVALID, "step: null argument");
+    DeviceGuard guard(b->device);
+    return step_impl(b, actions, dtype, on_device, device_api, auto_reset, static_cast<cudaStream_t>(stream), nullptr,
+                     nullptr);
+}
+
+int nesle_step_profile(nesle_batch* b, const void* actions, int dtype, int on_device, void* stream,
+                       uint64_t* opcode_counts, uint64_t* pc_counts) {
+    if (!b) return fail(NESLE_ERR_INVALID, "step_profile: null argument");
+    DeviceGuard guard(b->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    if (!b->d_prof) TRY(b->alloc(&b->d_prof, 256 + 65536, "profile histograms"));
+    CUDA_TRY(cudaMemsetAsync(b->d_prof, 0, (256 + 65536) * sizeof(unsigned long long), s), "clear profile");
+    TRY(step_impl(b, actions, dtype, on_device, 0, 0, s, b->d_prof, b->d_prof + 256));
+    if (opcode_counts)
+        CUDA_TRY(cudaMemcpyAsync(opcode_counts, b->d_prof, 256 * sizeof(uint64_t), cudaMemcpyDeviceToHost, s),
+                 "copy opcode profile");
+    if (pc_counts)
+        CUDA_TRY(cudaMemcpyAsync(pc_counts, b->d_prof + 256, 65536 * sizeof(uint64_t), cudaMemcpyDeviceToHost, s),
+                 "copy pc profile");
+    CUDA_TRY(cudaStreamSynchronize(s), "step profile synchronize");
+    return NESLE_OK;
 }
 
 static int ensure_frames(nesle_batch* b, int which) {

@@ -98,15 +98,34 @@ step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
 }
 
 // --------------------------------------------------------------------------
-// Env step, RAM in place.  The env's RAM row stays in global memory (L2
-// resident for moderate batches) and only PRG + decode table are staged, so a
-// CTA is 256 envs and every env of a 65,536-env batch is resident at once:
-// warp parallelism, not shared-memory latency, hides the memory latency.
+// Env step, RAM in place.  The env's RAM row stays in global memory and only
+// PRG + execution entries are staged, so a CTA holds up to 448 envs and every
+// env of a 65,536-env batch is resident at once (one CTA per SM): warp
+// parallelism, not shared-memory capacity, hides the memory latency.
+// kProfile adds the step_profile histograms: opcode counts gathered per CTA in
+// shared memory, fetch-address counts with warp-aggregated global atomics.
 // --------------------------------------------------------------------------
+struct DeviceProfile {
+    uint32_t* op_counts;             // shared, 256
+    unsigned long long* pc_counts;   // global, 65536
+    NESLE_HD void count(uint32_t op, uint32_t pc) const {
+#if defined(__CUDA_ARCH__)
+        const uint32_t active = __activemask(), lane = threadIdx.x & 31u;
+        uint32_t peers = __match_any_sync(active, op);
+        if (lane == (uint32_t)(__ffs(peers) - 1)) atomicAdd(&op_counts[op], (uint32_t)__popc(peers));
+        peers = __match_any_sync(active, pc);
+        if (lane == (uint32_t)(__ffs(peers) - 1)) atomicAdd(&pc_counts[pc], (unsigned long long)__popc(peers));
+#endif
+    }
+};
+
+template <bool kProfile>
 __global__ void __launch_bounds__(kGlobalMaxThreads, 1)
 step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
-                   const long long* __restrict__ act64, uint32_t flags) {
+                   const long long* __restrict__ act64, uint32_t flags, unsigned long long* __restrict__ prof_op,
+                   unsigned long long* __restrict__ prof_pc) {
     extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ uint32_t s_op[kProfile ? 256 : 1];
     uint8_t* s_prg = smem;
     Entry* s_dec = reinterpret_cast<Entry*>(smem + kPrgSmem);
     const BatchView& v = *vp;
@@ -116,34 +135,42 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
     if (tid == 0) reinterpret_cast<uint4*>(s_prg)[2048] = make_uint4(0, 0, 0, 0);
     const uint4* ent_src = reinterpret_cast<const uint4*>(&kEntriesConst);
     for (uint32_t i = tid; i < kDecSmem / 16; i += blockDim.x) reinterpret_cast<uint4*>(s_dec)[i] = ent_src[i];
+    if (kProfile)
+        for (uint32_t i = tid; i < 256; i += blockDim.x) s_op[i] = 0;
     __syncthreads();
     const uint32_t env = blockIdx.x * blockDim.x + tid;
-    if (env >= v.num_envs) return;
+    if (env < v.num_envs) {
+        Ctx c;
+        c.ram = v.ram + (size_t)env * kRamBytes;
+        c.slots = 1;
+        c.prg = s_prg;
+        c.dec = s_dec;
+        c.view = vp;
+        c.env = env;
+        c.frameskip = v.frameskip;
+        c.max_instr = v.max_instructions;
+        c.prg_ram = v.prg_ram + (size_t)env * kPrgRamBytes;
+        c.nt = v.nt + (size_t)env * kNtBytes;
+        c.pal = v.pal + (size_t)env * kPalBytes;
+        c.oam = v.oam + (size_t)env * kOamBytes;
 
-    Ctx c;
-    c.ram = v.ram + (size_t)env * kRamBytes;
-    c.slots = 1;
-    c.prg = s_prg;
-    c.dec = s_dec;
-    c.view = vp;
-    c.env = env;
-    c.frameskip = v.frameskip;
-    c.max_instr = v.max_instructions;
-    c.prg_ram = v.prg_ram + (size_t)env * kPrgRamBytes;
-    c.nt = v.nt + (size_t)env * kNtBytes;
-    c.pal = v.pal + (size_t)env * kPalBytes;
-    c.oam = v.oam + (size_t)env * kOamBytes;
-
-    EnvRecord rec = v.rec[env];
-    const uint32_t status_before = rec.status;
-    const uint8_t action = act64 ? (uint8_t)(act64[env] & 0xFF) : act8[env];
-    float reward;
-    uint8_t done;
-    run_env_step<false>(c, rec, action, reward, done);
-    const bool faulted = finish_env(v, env, rec, status_before, reward, done, flags & kStepDeviceApi,
-                                    flags & kStepAutoReset);
-    v.rec[env] = rec;
-    if (faulted) atomicAdd(v.fault_count, 1u);
+        EnvRecord rec = v.rec[env];
+        const uint32_t status_before = rec.status;
+        const uint8_t action = act64 ? (uint8_t)(act64[env] & 0xFF) : act8[env];
+        float reward;
+        uint8_t done;
+        if (kProfile) run_env_step<false>(c, rec, action, reward, done, DeviceProfile{s_op, prof_pc});
+        else run_env_step<false>(c, rec, action, reward, done);
+        const bool faulted = finish_env(v, env, rec, status_before, reward, done, flags & kStepDeviceApi,
+                                        flags & kStepAutoReset);
+        v.rec[env] = rec;
+        if (faulted) atomicAdd(v.fault_count, 1u);
+    }
+    if (kProfile) {
+        __syncthreads();
+        for (uint32_t i = tid; i < 256; i += blockDim.x)
+            if (s_op[i]) atomicAdd(&prof_op[i], (unsigned long long)s_op[i]);
+    }
 }
 
 // --------------------------------------------------------------------------
@@ -314,10 +341,15 @@ uint32_t global_step_threads(uint32_t num_envs, uint32_t num_sms) {
 }
 
 cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* act8, const long long* act64,
-                        uint32_t flags, uint32_t variant, uint32_t threads, cudaStream_t s) {
-    if (variant == kStepGlobalRam) {
+                        uint32_t flags, uint32_t variant, uint32_t threads, cudaStream_t s,
+                        unsigned long long* prof_op, unsigned long long* prof_pc) {
+    if (prof_op || prof_pc) {  // step_profile: the in-place kernel with histograms
+        if (!prof_op || !prof_pc) return cudaErrorInvalidValue;
         const uint32_t blocks = (num_envs + threads - 1) / threads;
-        step_kernel_global<<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags);
+        step_kernel_global<true><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags, prof_op, prof_pc);
+    } else if (variant == kStepGlobalRam) {
+        const uint32_t blocks = (num_envs + threads - 1) / threads;
+        step_kernel_global<false><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags, nullptr, nullptr);
     } else {
         const uint32_t blocks = (num_envs + kStepSlots - 1) / kStepSlots;
         step_kernel<<<blocks, kStepSlots, step_smem_bytes(), s>>>(dv, act8, act64, flags);

@@ -18,8 +18,10 @@ enum : uint32_t { kStepDeviceApi = 1, kStepAutoReset = 2 };
 size_t step_smem_bytes();
 cudaError_t configure_kernels();
 uint32_t global_step_threads(uint32_t num_envs, uint32_t num_sms);
+// prof_op (256) / prof_pc (65536): step_profile histograms to add to, or both null.
 cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* act8, const long long* act64,
-                        uint32_t flags, uint32_t variant, uint32_t threads, cudaStream_t s);
+                        uint32_t flags, uint32_t variant, uint32_t threads, cudaStream_t s,
+                        unsigned long long* prof_op = nullptr, unsigned long long* prof_pc = nullptr);
 cudaError_t launch_reset(const BatchView* dv, uint32_t num_envs, const uint8_t* mask, bool full, cudaStream_t s);
 cudaError_t launch_poke(const BatchView* dv, uint32_t num_envs, uint32_t address, uint32_t value, cudaStream_t s);
 cudaError_t launch_render(const BatchView* dv, uint32_t num_envs, uint8_t* out, int mode, cudaStream_t s);

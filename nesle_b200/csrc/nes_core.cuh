@@ -990,8 +990,15 @@ NESLE_HD void begin_step(Lane& L) {
 // All frames of one env-step: step_batch_console_instruction_lazy
 // (batch_console.hpp:77-109) per iteration, with the loop-top bookkeeping,
 // NMI entry and bus fetches on the rare path.
-template <bool kSharedRam>
-NESLE_HD void run_frames(const Ctx& c, Lane& L) {
+// Instruction histograms (step_profile): a profiler's count(opcode, pc) is
+// called once per executed instruction with its opcode and the address it was
+// fetched from (kernels.cu:59-64).  NoProfile compiles to nothing.
+struct NoProfile {
+    NESLE_HD void count(uint32_t, uint32_t) const {}
+};
+
+template <bool kSharedRam, class Prof = NoProfile>
+NESLE_HD void run_frames(const Ctx& c, Lane& L, const Prof& prof = Prof()) {
     Fetched f{};
     bool fresh = false;
     for (;;) {
@@ -1025,6 +1032,7 @@ NESLE_HD void run_frames(const Ctx& c, Lane& L) {
         } else {
             it_cyc += exec_uniform<kSharedRam>(c, L, f, fresh);
         }
+        prof.count(op, pc);
         it_cyc += L.dma;
         L.dma = 0;
         L.cycles += it_cyc;
@@ -1145,12 +1153,13 @@ NESLE_HD void seed_presentation(const BatchView& v, uint32_t env, EnvRecord& r) 
 
 // Runs env `c.env` for one env-step (frameskip frames).  Its RAM must be
 // staged at `c.ram`; `rec` is updated in place.
-template <bool kSharedRam = true>
-NESLE_HD void run_env_step(const Ctx& c, EnvRecord& rec, uint8_t action, float& reward, uint8_t& done) {
+template <bool kSharedRam = true, class Prof = NoProfile>
+NESLE_HD void run_env_step(const Ctx& c, EnvRecord& rec, uint8_t action, float& reward, uint8_t& done,
+                           const Prof& prof = Prof()) {
     Lane L;
     load_lane(L, rec, action);
     begin_step(L);
-    run_frames<kSharedRam>(c, L);
+    run_frames<kSharedRam>(c, L, prof);
     reward_done(c, L, reward, done);
     store_lane(L, rec);
 }

@@ -105,6 +105,7 @@ class Oracle(_Base):
                                              ctypes.c_uint32]
             lib.oracle_trace_count.restype = ctypes.c_uint32
             lib.oracle_trace_count.argtypes = [ctypes.c_void_p]
+            lib.oracle_set_profile.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
             lib.oracle_counter_rand.restype = ctypes.c_uint64
             lib.oracle_counter_rand.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64,
                                                 ctypes.c_uint64]
@@ -144,6 +145,17 @@ class Oracle(_Base):
 
     def poke_ram(self, address: int, value: int) -> None:
         self.lib().oracle_poke_ram(self._h, address, value)
+
+    def step_profile(self, actions: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+        """Host step (no auto-reset) returning the (256,) opcode and (65536,)
+        fetch-address histograms of its instructions."""
+        ops, pcs = np.zeros(256, np.uint64), np.zeros(65536, np.uint64)
+        self.lib().oracle_set_profile(self._h, ops.ctypes.data, pcs.ctypes.data)
+        try:
+            self.step(actions, device_api=False, auto_reset=False)
+        finally:
+            self.lib().oracle_set_profile(self._h, None, None)
+        return ops, pcs
 
     TRACE_DTYPE = np.dtype([("pc", "<u2"), ("op", "u1"), ("a", "u1"), ("x", "u1"), ("y", "u1"),
                             ("p", "u1"), ("sp", "u1"), ("cycles", "<u8")])
@@ -218,6 +230,8 @@ class Reference(_Base):
             lib.ref_get_field.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p]
             lib.ref_decode_table.argtypes = [_u8p, _u8p, _u8p]
             lib.ref_parse_fcs.argtypes = [_u8p, ctypes.c_size_t, ctypes.POINTER(RefFcs)]
+            lib.ref_set_profile.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+            lib.ref_set_profile.restype = ctypes.c_int
             for f in ("ref_reset", "ref_reset_envs", "ref_step", "ref_render_rgb", "ref_get_field",
                       "ref_parse_fcs"):
                 getattr(lib, f).restype = ctypes.c_int
@@ -261,6 +275,16 @@ class Reference(_Base):
         a = np.ascontiguousarray(actions, dtype=np.uint8)
         assert a.shape == (self.num_envs,)
         self._check(self.lib().ref_step(self._h, _as_u8(a), int(device_api), int(auto_reset), self.threads))
+
+    def step_profile(self, actions: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+        """Kind B: host step with the reference kernel's opcode / PC histograms."""
+        ops, pcs = np.zeros(256, np.uint64), np.zeros(65536, np.uint64)
+        self._check(self.lib().ref_set_profile(self._h, ops.ctypes.data, pcs.ctypes.data))
+        try:
+            self.step(actions, device_api=False, auto_reset=False)
+        finally:
+            self._check(self.lib().ref_set_profile(self._h, None, None))
+        return ops, pcs
 
     def render_rgb(self) -> np.ndarray:
         out = np.zeros((self.num_envs, 240, 256, 3), np.uint8)

@@ -150,6 +150,7 @@ struct nes_oracle {
     env_t *env;
     uint32_t trace_env, trace_cap, trace_n;
     uint8_t *trace_buf;
+    uint64_t *prof_opcode, *prof_pc; /* step_profile histograms (256, 65536) or NULL */
 };
 
 static __thread char g_err[256];
@@ -826,6 +827,10 @@ static void env_step(const nes_oracle *o, env_t *e, uint32_t env) {
             }
             pending += (uint32_t)(e->cycles - before) * 3u;
             ++instr;
+            /* kernels.cu:59-64: one count per executed instruction, by opcode
+             * and by the address it was fetched from (after any NMI entry). */
+            if (o->prof_opcode) o->prof_opcode[opc]++;
+            if (o->prof_pc) o->prof_pc[op_pc]++;
             if (o->trace_buf && env == o->trace_env && o->trace_n < o->trace_cap) {
                 uint8_t *r = ((nes_oracle *)o)->trace_buf + (size_t)o->trace_n * 16;
                 r[0] = (uint8_t)op_pc; r[1] = (uint8_t)(op_pc >> 8); r[2] = (uint8_t)opc;
@@ -915,6 +920,11 @@ void oracle_set_trace(nes_oracle *o, uint32_t env, uint8_t *buf, uint32_t cap) {
     o->trace_env = env; o->trace_buf = buf; o->trace_cap = cap; o->trace_n = 0;
 }
 uint32_t oracle_trace_count(const nes_oracle *o) { return o->trace_n; }
+
+void oracle_set_profile(nes_oracle *o, uint64_t *opcode_counts, uint64_t *pc_counts) {
+    o->prof_opcode = opcode_counts;
+    o->prof_pc = pc_counts;
+}
 
 void oracle_reset(nes_oracle *o) {
     for (uint32_t i = 0; i < o->n; ++i) {

@@ -71,6 +71,11 @@ uint32_t oracle_num_envs(const nes_oracle *o);
 void oracle_set_trace(nes_oracle *o, uint32_t env, uint8_t *buf, uint32_t cap);
 uint32_t oracle_trace_count(const nes_oracle *o);
 
+/* step_profile histograms (cuda_module.cu:734-818): while set, every executed
+ * instruction adds one to opcode_counts[opcode] (256 entries) and to
+ * pc_counts[address] (65536 entries).  The caller clears them.  NULL stops. */
+void oracle_set_profile(nes_oracle *o, uint64_t *opcode_counts, uint64_t *pc_counts);
+
 /* Decode-table export for pinning: per opcode {mode, base_cycles, flags}. */
 void oracle_decode_table(uint8_t *mode, uint8_t *base_cycles, uint8_t *flags);
 

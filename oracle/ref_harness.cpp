@@ -89,6 +89,8 @@ struct BatchB {
     V<std::uint64_t> b_cycles;
     nesle::cuda::BatchBuffers buf{};
     nesle::cuda::SnapshotTemplate bank{};
+    std::uint64_t* prof_opcode = nullptr;  // kernels.cu:59-64 histograms, when set
+    std::uint64_t* prof_pc = nullptr;
 
     void allocate() {
         const std::size_t n = cfg.n;
@@ -206,6 +208,8 @@ struct BatchB {
                 }
                 const auto s = step_batch_console_instruction_lazy(buf, env, state, hot);
                 pending += s.ppu_cycles;
+                if (prof_opcode) ++prof_opcode[s.cpu.opcode];
+                if (prof_pc) ++prof_pc[s.cpu.pc];
                 ++instr;
                 if (s.cpu.opcode == 0x4C && state.pc == s.cpu.pc && frames_done == 0) {
                     frames_done += batch_ppu_step_env_hot(buf, env, pending, hot).frames_completed;
@@ -446,6 +450,17 @@ int ref_step(void* hv, const std::uint8_t* actions, int device_api, int auto_res
     return guarded([&] {
         if (h->b) h->b->step(actions, device_api, auto_reset);
         else h->a->step(actions, device_api, auto_reset, threads);
+    });
+}
+
+// Kind B only: opcode / fetch-address histograms of the following steps, as
+// console_step_kernel counts them (kernels.cu:59-64).  NULL stops counting.
+int ref_set_profile(void* hv, std::uint64_t* opcode_counts, std::uint64_t* pc_counts) {
+    auto* h = static_cast<Handle*>(hv);
+    return guarded([&] {
+        if (!h->b) throw std::invalid_argument("profiling is only available for kind B");
+        h->b->prof_opcode = opcode_counts;
+        h->b->prof_pc = pc_counts;
     });
 }
 

@@ -217,3 +217,33 @@ def test_illegal_opcode_raises_runtime_error(torch):
     b = CudaBatch(4, 2, rom, device=0)
     with pytest.raises(RuntimeError, match="illegal 6502 opcode 0x02"):
         b.step(np.zeros(4, np.uint8), render_frame=False, copy_obs=False)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("make", [w.config1, w.config3, w.config4])
+def test_step_profile_histograms_match_checker(torch, make):
+    """step_profile: stats and the opcode / fetch-address histograms, exact (200 envs: several
+    warps, lanes of one warp at the same and at different addresses)."""
+    from nesle_b200._cuda_core import CudaBatch
+    from oracle import Oracle
+
+    wl = make()
+    n = 200
+    env = np.arange(n)
+    e2l = wl.env_to_level(env) if wl.env_to_level else None
+    kw = dict(done_mode=wl.done_mode, done_args=wl.done_args, seed=wl.seed)
+    snaps = wl.snapshots if wl.snapshots else None
+    b = CudaBatch(n, wl.frameskip, wl.rom.image, snaps, e2l if snaps and len(snaps) > 1 else None, device=0, **kw)
+    o = Oracle(n, wl.frameskip, wl.rom.image, wl.snapshots, env_to_level=e2l, **kw)
+    for s in range(2):
+        a = wl.actions(env, s)
+        out = b.step_profile(a)
+        ops, pcs = o.step_profile(a)
+        np.testing.assert_array_equal(out["opcode_counts"], ops)
+        np.testing.assert_array_equal(out["pc_counts"], pcs)
+        np.testing.assert_array_equal(out["instructions"], o.get("stat_instructions"))
+        np.testing.assert_array_equal(out["rewards"], o.get("reward"))
+        assert int(out["opcode_counts"].sum()) == int(out["instructions"].sum())
+        b.step_device(torch.from_numpy(wl.actions(env, 10 + s)).cuda())  # unprofiled steps in between
+        o.step(wl.actions(env, 10 + s))
+

@@ -200,6 +200,26 @@ def test_checker_config3_frames_match_reference_rgb():
     assert (o.get("snap_sx_start") != o.get("snap_sx_end")).any()  # the split happened
 
 
+@needs_ref
+@pytest.mark.parametrize("make", [w.config1, w.config3, w.config4])
+def test_checker_profile_histograms_match_reference(make):
+    """step_profile: opcode and fetch-address histograms as console_step_kernel counts them."""
+    wl = make()
+    n = 6
+    env = np.arange(n)
+    e2l = wl.env_to_level(env) if wl.env_to_level else None
+    kw = dict(env_to_level=e2l, done_mode=wl.done_mode, done_args=wl.done_args, seed=wl.seed)
+    o = Oracle(n, 4, wl.rom.image, wl.snapshots, **kw)
+    r = Reference("B", n, 4, wl.rom.image, wl.snapshots, **kw)
+    for s in range(3):
+        a = wl.actions(env, s)
+        (oo, op), (ro, rp) = o.step_profile(a), r.step_profile(a)
+        np.testing.assert_array_equal(oo, ro)
+        np.testing.assert_array_equal(op, rp)
+        assert int(oo.sum()) == int(o.get("stat_instructions").sum()) > 0
+        o.step(a), r.step(a)  # and an ordinary step between profiles
+
+
 # --- 4. FCS parsing -------------------------------------------------------------
 
 @needs_ref
