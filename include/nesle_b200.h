@@ -98,6 +98,17 @@ int nesle_step_profile(nesle_batch* b, const void* actions, int action_dtype, in
 /* Replaces CudaBatch.render_device() (cuda_module.cu:860-863, 1435-1438). */
 int nesle_render(nesle_batch* b, int mode, void* stream);
 
+/* No counterpart in the reference.  The 84x84 grey observation of every env
+ * copied into `host_out` (num_envs * 7056 bytes), without allocating device
+ * memory: the kernel renders into a static device scratch of 1,024 envs
+ * (7,225,344 bytes, part of the library's module image) and the call copies
+ * it out and synchronizes.  Batches of more than 1,024 envs are rejected
+ * (NESLE_ERR_INVALID).  The scratch address is looked up once per device on
+ * the first call: make that first call before any stream capture.  The
+ * scratch is shared by all batches of a device, so concurrent calls race;
+ * serialise them. */
+int nesle_render_gray84_noalloc(nesle_batch* b, uint8_t* host_out, uint64_t bytes, void* stream);
+
 /* Replaces CudaBatch.poke_ram(address, value) (cuda_module.cu:939-945). */
 int nesle_poke_ram(nesle_batch* b, uint16_t address, uint8_t value, void* stream);
 

@@ -61,6 +61,8 @@ SIGNATURES = {
     "nesle_step_profile": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "nesle_render": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "nesle_render_gray84_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
+                                                   ctypes.c_void_p]),
     "nesle_poke_ram": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint16, ctypes.c_uint8, ctypes.c_void_p]),
     "nesle_device_ptr": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
                                         ctypes.POINTER(ctypes.c_uint64)]),

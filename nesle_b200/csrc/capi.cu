@@ -5,6 +5,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -86,6 +87,29 @@ struct nesle_batch {
         int rc_ = (expr);             \
         if (rc_ != NESLE_OK) return rc_; \
     } while (0)
+
+// Static scratch of nesle_render_gray84_noalloc: 1,024 envs x 7,056 bytes
+// (7,225,344 B), part of the module image rather than a runtime allocation.
+constexpr uint32_t kNoAllocGrayEnvs = 1024;
+static __device__ __align__(256) uint8_t g_gray84_scratch[(size_t)kNoAllocGrayEnvs * kGray * kGray];
+constexpr int kNoAllocMaxDevices = 64;
+static std::mutex g_noalloc_mu;
+static uint8_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Address of the scratch on the current device (looked up once per device).
+static int noalloc_scratch(int device, uint8_t** out) {
+    if (device < 0 || device >= kNoAllocMaxDevices) return fail(NESLE_ERR_INVALID, "render_gray84_noalloc: device ordinal");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_gray84_scratch);
+        if (e != cudaSuccess)
+            return fail(NESLE_ERR_CUDA, std::string("render_gray84_noalloc scratch: ") + cudaGetErrorString(e));
+        g_noalloc_ptr[device] = static_cast<uint8_t*>(p);
+    }
+    *out = g_noalloc_ptr[device];
+    return NESLE_OK;
+}
 
 extern "C" {
 
@@ -484,6 +508,31 @@ int nesle_fault_count(nesle_batch* b, uint32_t* count) {
     DeviceGuard guard(b->device);
     CUDA_TRY(cudaEventSynchronize(b->done_event), "synchronize");
     CUDA_TRY(cudaMemcpy(count, b->hv.fault_count, sizeof(uint32_t), cudaMemcpyDeviceToHost), "copy fault count");
+    return NESLE_OK;
+}
+
+// No-allocation 84x84 observation: the render kernel writes into a file-scope
+// device scratch (module memory, set up once per device by
+// cudaGetSymbolAddress) and the result is copied to the caller's host buffer.
+// No cudaMalloc / cudaFree.  Concurrent calls on one device share the scratch
+// and race.  Every scratch byte the call reads is written by the kernel first,
+// so nothing needs clearing.
+int nesle_render_gray84_noalloc(nesle_batch* b, uint8_t* host_out, uint64_t bytes, void* stream) {
+    if (!b || !host_out) return fail(NESLE_ERR_INVALID, "render_gray84_noalloc: null argument");
+    if (b->n > kNoAllocGrayEnvs)
+        return fail(NESLE_ERR_INVALID, "render_gray84_noalloc: batch of " + std::to_string(b->n) +
+                                           " envs exceeds its static scratch (at most " +
+                                           std::to_string(kNoAllocGrayEnvs) + " envs)");
+    if (bytes != (uint64_t)b->n * kGray * kGray)
+        return fail(NESLE_ERR_INVALID, "render_gray84_noalloc: expected " + std::to_string((uint64_t)b->n * kGray * kGray) +
+                                           " bytes, got " + std::to_string(bytes));
+    DeviceGuard guard(b->device);
+    uint8_t* scratch = nullptr;
+    TRY(noalloc_scratch(b->device, &scratch));
+    auto s = static_cast<cudaStream_t>(stream);
+    CUDA_TRY(launch_render(b->dv, b->n, scratch, NESLE_RENDER_GRAY84, s), "render_gray84_noalloc kernel");
+    CUDA_TRY(cudaMemcpyAsync(host_out, scratch, bytes, cudaMemcpyDeviceToHost, s), "render_gray84_noalloc copy");
+    CUDA_TRY(cudaStreamSynchronize(s), "render_gray84_noalloc synchronize");
     return NESLE_OK;
 }
 
