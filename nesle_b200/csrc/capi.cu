@@ -267,14 +267,20 @@ static int create_impl(const nesle_create_args* a, nesle_batch* b) {
     v.actions = nullptr;
     TRY(b->alloc(&b->dv, 1, "batch view"));
     CUDA_TRY(cudaMemcpy(b->dv, &v, sizeof(BatchView), cudaMemcpyHostToDevice), "batch view upload");
-    // Step-kernel placement of env RAM (default: in place in global memory);
-    // NESLE_STEP_KERNEL=shared stages it in shared memory, 96 envs per SM.
+    // Step-kernel placement of env RAM.  Up to two waves of shared-memory CTAs
+    // (kStepSlots envs per SM per wave) the RAM is staged in shared memory: with
+    // few warps per SM the latency of each env's instruction chain decides, and
+    // shared memory has the shorter one (B200, config-4 workload: 185k vs 77k
+    // env-steps/s at 2,048 envs, 740k vs 592k at 16,384; in place wins from
+    // 32,768 on).  Larger batches keep RAM in place, every env resident.
+    // NESLE_STEP_KERNEL=shared|global overrides.
+    int sms = 0;
+    CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, a->device), "SM count");
+    b->step_variant = b->n <= 2u * (uint32_t)sms * kStepSlots ? kStepSharedRam : kStepGlobalRam;
     if (const char* sv = getenv("NESLE_STEP_KERNEL")) {
         if (strcmp(sv, "global") == 0) b->step_variant = kStepGlobalRam;
         else if (strcmp(sv, "shared") == 0) b->step_variant = kStepSharedRam;
     }
-    int sms = 0;
-    CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, a->device), "SM count");
     b->step_threads = global_step_threads(b->n, static_cast<uint32_t>(sms));
     CUDA_TRY(cudaEventCreateWithFlags(&b->done_event, cudaEventDisableTiming), "create event");
     CUDA_TRY(launch_reset(b->dv, b->n, nullptr, true, nullptr), "initial reset");
