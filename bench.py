@@ -352,7 +352,7 @@ def run_ours(args, rank, world, local) -> dict | None:
         peaks = measured_peaks()
         peak = float(peaks.get("hbm_gbs", 6650.0))
         sm_mhz = clock_summary.get("sm_mhz") or float(peaks.get("sm_max_mhz", 1965.0))
-        step_roof = {"kernel": "step_kernel_global", "bound": "hbm",
+        step_roof = {"kernel": f"step kernel ({batch.step_kernel_placement} RAM placement)", "bound": "hbm",
                      "achieved": BYTES_PER_ENV_STEP * n / (kernel_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                      "traffic": profile_traffic(), "ms": kernel_ms,
                      "note": "of measured HBM copy bandwidth; the kernel is latency/issue-bound (see issue)"}
@@ -482,7 +482,7 @@ def run_ppo(args, rank, world, local) -> dict | None:
         update_flops = 6.0 * params * cfg.num_envs * cfg.n_steps * cfg.update_epochs
         tflops = update_flops / (update_ms / 1e3) / 1e12
         bf16_peak = float(peaks.get("bf16_tflops", 1590.0))
-        step_roof = {"kernel": "step_kernel_global", "bound": "hbm",
+        step_roof = {"kernel": f"step kernel ({tr.batch.step_kernel_placement} RAM placement)", "bound": "hbm",
                      "achieved": BYTES_PER_ENV_STEP * cfg.num_envs / (kernel_ms / 1e3) / 1e9, "peak": hbm,
                      "unit": "GB/s", "traffic": None, "ms": kernel_ms,
                      "note": "of measured HBM copy bandwidth; at 2,048 envs the kernel is bound by the latency "

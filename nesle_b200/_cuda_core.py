@@ -330,6 +330,19 @@ class CudaBatch:
         return self._num_levels
 
     # -- extensions -------------------------------------------------------
+    @property
+    def step_kernel_placement(self) -> str:
+        """Where the step kernel keeps env RAM: "shared" (staged in shared memory),
+        "hybrid" (in place, zero page in shared memory) or "global" (in place)."""
+        info = _lib.Info()
+        self._check(self._lib.nesle_get_info(self._h, ctypes.byref(info)))
+        staging = 32768 + 16 + 256 * 32  # PRG + execution entries
+        if info.smem_bytes_per_block == staging:
+            return "global"
+        if info.smem_bytes_per_block == staging + info.envs_per_block * 256:
+            return "hybrid"
+        return "shared"
+
     def frames_index_device(self, render: bool = True) -> CudaDeviceArrayView:
         if render:
             self._check(self._lib.nesle_render(self._h, _lib.RENDER_INDEX, ctypes.c_void_p(self._stream())))

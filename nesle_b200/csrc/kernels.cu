@@ -7,6 +7,7 @@
 //   render_kernel   colour index or RGB per pixel from the presentation snapshot
 //   gray84_kernel   84x84 area-resampled luma observation
 #include <cuda_runtime.h>
+#include <stdlib.h>
 
 #include "kernels.h"
 #include "nes_core.cuh"
@@ -67,6 +68,8 @@ step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
     Ctx c;
     c.ram = slot;
     c.slots = kStepSlots;
+    c.zp = nullptr;
+    c.zslots = 0;
     c.prg = s_prg;
     c.dec = s_dec;
     c.view = vp;
@@ -119,7 +122,12 @@ struct DeviceProfile {
     }
 };
 
-template <bool kProfile>
+// kHybrid: each env's zero page ($0000-$00FF) is staged into shared memory for
+// the launch (interleaved 4 bytes per lane: every lane keeps to its own bank)
+// and written back before the env's done/auto-reset; the rest of RAM stays in
+// place.  Zero-page operands and indirect pointers then cost a shared-memory
+// access instead of a global one.
+template <bool kProfile, bool kHybrid>
 __global__ void __launch_bounds__(kGlobalMaxThreads, 1)
 step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
                    const long long* __restrict__ act64, uint32_t flags, unsigned long long* __restrict__ prof_op,
@@ -128,6 +136,7 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
     __shared__ uint32_t s_op[kProfile ? 256 : 1];
     uint8_t* s_prg = smem;
     Entry* s_dec = reinterpret_cast<Entry*>(smem + kPrgSmem);
+    uint32_t* s_zp = reinterpret_cast<uint32_t*>(smem + kPrgSmem + kDecSmem);  // [64 words][blockDim lanes]
     const BatchView& v = *vp;
     const uint32_t tid = threadIdx.x;
     const uint4* prg_src = reinterpret_cast<const uint4*>(v.prg);
@@ -143,6 +152,21 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
         Ctx c;
         c.ram = v.ram + (size_t)env * kRamBytes;
         c.slots = 1;
+        c.zp = nullptr;
+        c.zslots = 0;
+        if (kHybrid) {
+            const uint4* src = reinterpret_cast<const uint4*>(c.ram);
+#pragma unroll 4
+            for (uint32_t q = 0; q < 16; ++q) {
+                const uint4 w = src[q];
+                s_zp[(4 * q + 0) * blockDim.x + tid] = w.x;
+                s_zp[(4 * q + 1) * blockDim.x + tid] = w.y;
+                s_zp[(4 * q + 2) * blockDim.x + tid] = w.z;
+                s_zp[(4 * q + 3) * blockDim.x + tid] = w.w;
+            }
+            c.zp = reinterpret_cast<uint8_t*>(s_zp + tid);
+            c.zslots = blockDim.x;
+        }
         c.prg = s_prg;
         c.dec = s_dec;
         c.view = vp;
@@ -161,6 +185,13 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
         uint8_t done;
         if (kProfile) run_env_step<false>(c, rec, action, reward, done, DeviceProfile{s_op, prof_pc});
         else run_env_step<false>(c, rec, action, reward, done);
+        if (kHybrid) {  // back in place before a possible auto-reset rewrites the row
+            uint4* dst = reinterpret_cast<uint4*>(c.ram);
+#pragma unroll 4
+            for (uint32_t q = 0; q < 16; ++q)
+                dst[q] = make_uint4(s_zp[(4 * q + 0) * blockDim.x + tid], s_zp[(4 * q + 1) * blockDim.x + tid],
+                                    s_zp[(4 * q + 2) * blockDim.x + tid], s_zp[(4 * q + 3) * blockDim.x + tid]);
+        }
         const bool faulted = finish_env(v, env, rec, status_before, reward, done, flags & kStepDeviceApi,
                                         flags & kStepAutoReset);
         v.rec[env] = rec;
@@ -325,8 +356,15 @@ gray84_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out) {
 // --------------------------------------------------------------------------
 size_t step_smem_bytes() { return kPrgSmem + kDecSmem + (size_t)kStepSlots * kRamBytes; }
 
+constexpr size_t kHybridSmemMax = kPrgSmem + kDecSmem + (size_t)kGlobalMaxThreads * 256;
+
 cudaError_t configure_kernels() {
-    return cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)step_smem_bytes());
+    cudaError_t e = cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)step_smem_bytes());
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(step_kernel_global<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kHybridSmemMax);
+    if (e != cudaSuccess) return e;
+    return e;
 }
 
 // Threads per in-place step CTA: one CTA per SM when the batch fits in one
@@ -346,10 +384,16 @@ cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* a
     if (prof_op || prof_pc) {  // step_profile: the in-place kernel with histograms
         if (!prof_op || !prof_pc) return cudaErrorInvalidValue;
         const uint32_t blocks = (num_envs + threads - 1) / threads;
-        step_kernel_global<true><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags, prof_op, prof_pc);
+        step_kernel_global<true, false><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags, prof_op,
+                                                                                    prof_pc);
     } else if (variant == kStepGlobalRam) {
         const uint32_t blocks = (num_envs + threads - 1) / threads;
-        step_kernel_global<false><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags, nullptr, nullptr);
+        step_kernel_global<false, false><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags, nullptr,
+                                                                                      nullptr);
+    } else if (variant == kStepHybridRam) {
+        const uint32_t blocks = (num_envs + threads - 1) / threads;
+        step_kernel_global<false, true><<<blocks, threads, kPrgSmem + kDecSmem + (size_t)threads * 256, s>>>(
+            dv, act8, act64, flags, nullptr, nullptr);
     } else {
         const uint32_t blocks = (num_envs + kStepSlots - 1) / kStepSlots;
         step_kernel<<<blocks, kStepSlots, step_smem_bytes(), s>>>(dv, act8, act64, flags);

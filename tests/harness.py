@@ -125,6 +125,10 @@ class HostCoreGlobal(HostCore):
     global_ram = True
 
 
+class HostCoreHybrid(HostCore):
+    global_ram = 2  # in place, zero page in a separate slot
+
+
 class GpuCore(_Common):
     """libnesle_b200.so through its C ABI (host arrays in, host copies out)."""
 

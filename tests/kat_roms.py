@@ -58,7 +58,20 @@ NMI_ROM = rom_with({0x8000: asm(0x8000, ("LDA", w.IMM, 0x80), ("STA", w.ABS, 0x2
 DMA_ROM = rom_with({0x8000: asm(0x8000, ("LDA", w.IMM, 0x02), ("STA", w.ABS, 0x4014),
                                 ("JMP", w.ABS, 0x8005))})
 
+# OAM DMA from page $00 and from its mirror $08 ((page << 8) & $7FF = $000):
+# the source is the zero page.
+DMA_ZP_ROM = rom_with({0x8000: asm(0x8000, ("LDA", w.IMM, 0x00), ("STA", w.ABS, 0x4014), ("INC", w.ZP, 0x10),
+                                   ("LDA", w.IMM, 0x08), ("STA", w.ABS, 0x4014), ("JMP", w.ABS, 0x800C))})
+
 IDLE_ROM = rom_with({0x8000: asm(0x8000, ("JMP", w.ABS, 0x8000))})
+
+
+def dma_zp_snapshot() -> bytes:
+    """PC at $8000 with RAM $0000+i = 3 i + 1 (mod 256)."""
+    ram = bytearray(2048)
+    for i in range(256):
+        ram[i] = (3 * i + 1) & 0xFF
+    return w.write_fcs(w.Snapshot(pc=0x8000, cpu_ram=bytes(ram)))
 
 
 def dma_snapshot() -> bytes:

@@ -32,6 +32,7 @@ struct HostBatch {
     std::vector<uint8_t> bram, bprg, bnt, bpal, boam, e2l;
     uint32_t fault = 0;
     bool global_ram = false;  // run the in-place (global-RAM) variant of the core
+    bool hybrid = false;      // ... with the zero page in a separate slot (hybrid placement)
     std::vector<uint8_t> smem_ram = std::vector<uint8_t>(kSlots * kRamBytes);
 };
 
@@ -112,7 +113,11 @@ int host_create(const nesle_create_args* a, void** out) {
 
 void host_destroy(void* p) { delete static_cast<HostBatch*>(p); }
 
-void host_set_global_ram(void* p, int on) { static_cast<HostBatch*>(p)->global_ram = on != 0; }
+void host_set_global_ram(void* p, int on) {
+    auto* h = static_cast<HostBatch*>(p);
+    h->global_ram = on != 0;  // 1 in place, 2 in place with the zero page in a separate slot
+    h->hybrid = on == 2;
+}
 
 void host_reset(void* p) {
     auto* h = static_cast<HostBatch*>(p);
@@ -160,12 +165,21 @@ void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) 
         c.nt = h->v.nt + (size_t)e * kNtBytes;
         c.pal = h->v.pal + (size_t)e * kPalBytes;
         c.oam = h->v.oam + (size_t)e * kOamBytes;
+        c.zp = nullptr;
+        c.zslots = 0;
+        uint32_t zp[64];  // hybrid placement: this env's zero page as one lane of words
+        if (h->hybrid) {
+            memcpy(zp, h->ram.data() + (size_t)e * kRamBytes, 256);
+            c.zp = reinterpret_cast<uint8_t*>(zp);
+            c.zslots = 1;
+        }
         EnvRecord rec = h->rec[e];
         const uint32_t before = rec.status;
         float reward;
         uint8_t done;
         if (h->global_ram) {
             run_env_step<false>(c, rec, actions[e], reward, done);
+            if (h->hybrid) memcpy(h->ram.data() + (size_t)e * kRamBytes, zp, 256);
         } else {
             run_env_step<true>(c, rec, actions[e], reward, done);
             unstage(*h, e, slot);

@@ -98,6 +98,9 @@ def test_properties(torch):
     c = CudaBatch(4, 4, wl1.rom.image, device=0)
     assert not c.has_snapshot and c.num_levels == 0
     assert hasattr(b, "step_device") and hasattr(b, "ram_device")  # native_ppo's bridge check
+    assert b.step_kernel_placement == "shared"  # small batches stage RAM in shared memory
+    big = CudaBatch(40000, 4, wl1.rom.image, device=0)
+    assert big.step_kernel_placement == "hybrid"
 
 
 @pytest.mark.gpu
