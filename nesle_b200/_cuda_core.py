@@ -249,6 +249,14 @@ class CudaBatch:
         out["dones"] = self._field("done")
         return out
 
+    def step_launch(self, actions: Any) -> None:
+        """Extension: the kernel of step() on the current stream (host actions
+        copied in, no auto-reset, no result copies, no synchronisation); the
+        rewards / done arrays are then read through device_ptr views."""
+        a = self._host_actions(actions)
+        self._check(self._lib.nesle_step(self._h, a.ctypes.data, _lib.ACTIONS_U8, 0, 0, 0,
+                                         ctypes.c_void_p(self._stream())))
+
     def step_device(self, actions: Any, auto_reset: bool = True, synchronize: bool = True) -> dict:
         """Device-array step with fused auto-reset (cuda_module.cu:594-666)."""
         ptr, dtype = self._device_actions(actions)
