@@ -109,6 +109,25 @@ int nesle_render(nesle_batch* b, int mode, void* stream);
  * serialise them. */
 int nesle_render_gray84_noalloc(nesle_batch* b, uint8_t* host_out, uint64_t bytes, void* stream);
 
+/* Env state save / restore; the device-side capture and restore of
+ * device_reset.cuh:72-263 (capture_device_reset_snapshot /
+ * restore_device_reset_snapshot) over an index list.  A state is one flat
+ * blob of nesle_state_bytes() bytes: the env record (CPU and PPU registers,
+ * counters, controller, reward baselines, episode), RAM, PRG-RAM, nametables,
+ * palette, OAM, the presentation snapshot, and the reward/done words.
+ * save copies envs[0..count) into count consecutive blobs at `dst`; load
+ * writes blobs into envs (any env may receive any saved state).  Env lists
+ * and blobs may be host or device memory; host indices are range-checked
+ * (NESLE_ERR_INVALID), device indices past the batch are skipped.  With host
+ * blobs the call synchronises; with device blobs it is asynchronous on
+ * `stream`.  The blob layout is this library's and can change with
+ * nesle_abi_version(). */
+uint64_t nesle_state_bytes(void);
+int nesle_save_states(nesle_batch* b, const uint32_t* envs, uint32_t count, int envs_on_device, void* dst,
+                      int dst_on_device, void* stream);
+int nesle_load_states(nesle_batch* b, const uint32_t* envs, uint32_t count, int envs_on_device, const void* src,
+                      int src_on_device, void* stream);
+
 /* Replaces CudaBatch.poke_ram(address, value) (cuda_module.cu:939-945). */
 int nesle_poke_ram(nesle_batch* b, uint16_t address, uint8_t value, void* stream);
 

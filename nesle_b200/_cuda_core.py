@@ -338,6 +338,64 @@ class CudaBatch:
         return self._num_levels
 
     # -- extensions -------------------------------------------------------
+    def save_states(self, envs: Any, device: bool = False):
+        """Full states of `envs` (device_reset.cuh capture semantics) as a
+        (len(envs), state_bytes) uint8 array: numpy on the host, or with
+        ``device=True`` a CUDA tensor (no host round trip)."""
+        idx = np.ascontiguousarray(np.asarray(envs, dtype=np.uint32).ravel())
+        n = len(idx)
+        if device:
+            torch = _torch()
+            if torch is None:
+                import torch  # noqa: F811
+            out = torch.empty((n, _lib.STATE_BYTES), dtype=torch.uint8, device=f"cuda:{self.device}")
+            self._check(self._lib.nesle_save_states(self._h, idx.ctypes.data, n, 0, ctypes.c_void_p(out.data_ptr()),
+                                                    1, ctypes.c_void_p(self._stream())))
+            return out
+        out = np.empty((n, _lib.STATE_BYTES), np.uint8)
+        self._check(self._lib.nesle_save_states(self._h, idx.ctypes.data, n, 0, out.ctypes.data, 0,
+                                                ctypes.c_void_p(self._stream())))
+        return out
+
+    def load_states(self, envs: Any, states: Any) -> None:
+        """Write saved states (host array or CUDA tensor, one row per env) into
+        `envs`; any env may receive any state, of this batch or another one
+        built from the same ROM."""
+        idx = np.ascontiguousarray(np.asarray(envs, dtype=np.uint32).ravel())
+        n = len(idx)
+        if hasattr(states, "is_cuda") and states.is_cuda:
+            if tuple(states.shape) != (n, _lib.STATE_BYTES) or not states.is_contiguous():
+                raise ValueError(f"states must be a contiguous ({n}, {_lib.STATE_BYTES}) uint8 tensor")
+            self._check(self._lib.nesle_load_states(self._h, idx.ctypes.data, n, 0,
+                                                    ctypes.c_void_p(states.data_ptr()), 1,
+                                                    ctypes.c_void_p(self._stream())))
+            return
+        arr = np.ascontiguousarray(np.asarray(states, dtype=np.uint8))
+        if arr.shape != (n, _lib.STATE_BYTES):
+            raise ValueError(f"states must have shape ({n}, {_lib.STATE_BYTES})")
+        self._check(self._lib.nesle_load_states(self._h, idx.ctypes.data, n, 0, arr.ctypes.data, 0,
+                                                ctypes.c_void_p(self._stream())))
+
+    def save_fcs(self, env: int) -> bytes:
+        """FCEUX FCS save state of env `env` as it is now (the reference's
+        snapshot format: usable as a CudaBatch reset snapshot)."""
+        from .fcs import Snapshot, write_fcs
+
+        blob = self.save_states([env])[0]
+        rec = blob[:128].view(_lib.ENV_RECORD_DTYPE)[0]
+
+        def part(name: str) -> bytes:
+            off, size = _lib.STATE_PARTS[name]
+            return blob[off:off + size].tobytes()
+
+        return write_fcs(Snapshot(
+            pc=int(rec["pc"]), a=int(rec["a"]), x=int(rec["x"]), y=int(rec["y"]), sp=int(rec["sp"]),
+            p=int(rec["p"]), cpu_ram=part("ram"), prg_ram=part("prg_ram"), ppu_ctrl=int(rec["ppu_ctrl"]),
+            ppu_mask=int(rec["ppu_mask"]), ppu_status=int(rec["ppu_status"]), ppu_oam_addr=int(rec["oam_addr"]),
+            ppu_open_bus=int(rec["open_bus"]), ppu_read_buffer=int(rec["read_buffer"]), ppu_x=int(rec["fine_x"]),
+            ppu_w=int(rec["w"]), ppu_v=int(rec["v"]), ppu_t=int(rec["t"]), nametable_ram=part("nametable"),
+            palette_ram=part("palette"), oam=part("oam")))
+
     @property
     def step_kernel_placement(self) -> str:
         """Where the step kernel keeps env RAM: "shared" (staged in shared memory),

@@ -60,6 +60,11 @@ SIGNATURES = {
                                   ctypes.c_int, ctypes.c_void_p]),
     "nesle_step_profile": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "nesle_state_bytes": (ctypes.c_uint64, []),
+    "nesle_save_states": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int,
+                                         ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "nesle_load_states": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int,
+                                         ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "nesle_render": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "nesle_render_gray84_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
                                                    ctypes.c_void_p]),
@@ -75,6 +80,22 @@ SIGNATURES = {
     "nesle_last_error": (ctypes.c_char_p, []),
     "nesle_abi_version": (ctypes.c_int, []),
 }
+
+# EnvRecord (csrc/nesle_state.h), the first 128 bytes of a saved state blob.
+ENV_RECORD_DTYPE = np.dtype({
+    "names": ["pc", "a", "x", "y", "sp", "p", "nmi_pending", "cycles", "frame", "frame_dot", "ppu_ctrl",
+              "ppu_mask", "ppu_status", "oam_addr", "v", "t", "fine_x", "w", "open_bus", "read_buffer",
+              "scroll_x", "scroll_y", "prev_x", "prev_time", "episode", "status"],
+    "formats": ["<u2", "u1", "u1", "u1", "u1", "u1", "u1", "<u8", "<u8", "<u4", "u1", "u1", "u1", "u1", "<u2",
+                "<u2", "u1", "u1", "u1", "u1", "u1", "u1", "<i4", "<i4", "<u4", "<u4"],
+    "offsets": [0, 2, 3, 4, 5, 6, 7, 8, 16, 24, 28, 29, 30, 31, 32, 34, 36, 37, 38, 39, 40, 41, 56, 60, 68, 72],
+    "itemsize": 128})
+
+# Saved-state blob parts: name -> (offset, bytes); see nesle_save_states.
+STATE_PARTS = {"rec": (0, 128), "ram": (128, 2048), "prg_ram": (2176, 8192), "nametable": (10368, 2048),
+               "palette": (12416, 32), "oam": (12448, 256), "snap_nametable": (12704, 2048),
+               "snap_palette": (14752, 32), "snap_oam": (14784, 256), "out": (15040, 16)}
+STATE_BYTES = 15056
 
 # Per-env fields of nesle_copy_field: name -> (dtype, per-env shape).
 FIELDS: dict[str, tuple[type, tuple[int, ...]]] = {

@@ -61,6 +61,9 @@ struct nesle_batch {
     uint8_t* d_frames_index = nullptr;
     uint8_t* d_gray84 = nullptr;
     unsigned long long* d_prof = nullptr;  // step_profile histograms: 256 opcode + 65536 PC counts
+    uint32_t* d_state_envs = nullptr;      // staging of host env lists / state blobs (grown on demand)
+    uint8_t* d_state_blobs = nullptr;
+    uint32_t state_cap = 0;
     cudaEvent_t done_event = nullptr;
     uint32_t step_variant = kStepGlobalRam;
     uint32_t step_threads = 0;
@@ -412,6 +415,54 @@ int nesle_render(nesle_batch* b, int mode, void* stream) {
     uint8_t* out = mode == NESLE_RENDER_RGB ? b->d_frames_rgb : mode == NESLE_RENDER_INDEX ? b->d_frames_index : b->d_gray84;
     auto s = static_cast<cudaStream_t>(stream);
     return finish(b, s, launch_render(b->dv, b->n, out, mode, s), "render kernel");
+}
+
+uint64_t nesle_state_bytes(void) { return kStateBytes; }
+
+static int state_io(nesle_batch* b, const uint32_t* envs, uint32_t count, int envs_on_device, void* blobs,
+                    int blobs_on_device, bool save, void* stream) {
+    if (!b || (count && (!envs || !blobs))) return fail(NESLE_ERR_INVALID, "state: null argument");
+    DeviceGuard guard(b->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    if (!envs_on_device)
+        for (uint32_t i = 0; i < count; ++i)
+            if (envs[i] >= b->n)
+                return fail(NESLE_ERR_INVALID, "env index " + std::to_string(envs[i]) + " out of range (batch of " +
+                                                   std::to_string(b->n) + ")");
+    if ((!envs_on_device || !blobs_on_device) && count > b->state_cap) {
+        // staging grows to the largest request (one allocation per growth, freed with the batch)
+        TRY(b->alloc(&b->d_state_envs, count, "state env list"));
+        TRY(b->alloc(&b->d_state_blobs, (size_t)count * kStateBytes, "state blobs"));
+        b->state_cap = count;
+    }
+    const uint32_t* d_envs = static_cast<const uint32_t*>(static_cast<const void*>(envs));
+    if (!envs_on_device) {
+        CUDA_TRY(cudaMemcpyAsync(b->d_state_envs, envs, count * sizeof(uint32_t), cudaMemcpyHostToDevice, s),
+                 "copy env list");
+        d_envs = b->d_state_envs;
+    }
+    uint8_t* d_blobs = blobs_on_device ? static_cast<uint8_t*>(blobs) : b->d_state_blobs;
+    if (!save && !blobs_on_device)
+        CUDA_TRY(cudaMemcpyAsync(d_blobs, blobs, (size_t)count * kStateBytes, cudaMemcpyHostToDevice, s),
+                 "copy state blobs");
+    TRY(finish(b, s, launch_state(b->dv, d_envs, count, d_blobs, save, s), save ? "save states" : "load states"));
+    if (save && !blobs_on_device) {
+        CUDA_TRY(cudaMemcpyAsync(blobs, d_blobs, (size_t)count * kStateBytes, cudaMemcpyDeviceToHost, s),
+                 "copy state blobs");
+        CUDA_TRY(cudaStreamSynchronize(s), "save states synchronize");
+    }
+    if (!save && !blobs_on_device) CUDA_TRY(cudaStreamSynchronize(s), "load states synchronize");
+    return NESLE_OK;
+}
+
+int nesle_save_states(nesle_batch* b, const uint32_t* envs, uint32_t count, int envs_on_device, void* dst,
+                      int dst_on_device, void* stream) {
+    return state_io(b, envs, count, envs_on_device, dst, dst_on_device, true, stream);
+}
+
+int nesle_load_states(nesle_batch* b, const uint32_t* envs, uint32_t count, int envs_on_device, const void* src,
+                      int src_on_device, void* stream) {
+    return state_io(b, envs, count, envs_on_device, const_cast<void*>(src), src_on_device, false, stream);
 }
 
 int nesle_poke_ram(nesle_batch* b, uint16_t address, uint8_t value, void* stream) {

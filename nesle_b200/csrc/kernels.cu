@@ -205,6 +205,53 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
 }
 
 // --------------------------------------------------------------------------
+// Env state save / load: one CTA per listed env copies its rows to or from a
+// kStateBytes blob with 16-byte accesses.  Indices past the batch are skipped.
+// --------------------------------------------------------------------------
+__device__ __forceinline__ void copy_part(uint8_t* blob, uint8_t* row, uint32_t bytes, bool save) {
+    uint4* b = reinterpret_cast<uint4*>(blob);
+    uint4* r = reinterpret_cast<uint4*>(row);
+    for (uint32_t i = threadIdx.x; i < bytes / 16; i += blockDim.x) {
+        if (save) b[i] = r[i];
+        else r[i] = b[i];
+    }
+}
+
+__global__ void __launch_bounds__(128)
+state_kernel(const BatchView* __restrict__ vp, const uint32_t* __restrict__ envs, uint8_t* __restrict__ blobs,
+             uint32_t save) {
+    const BatchView& v = *vp;
+    const uint32_t env = envs[blockIdx.x];
+    if (env >= v.num_envs) return;
+    uint8_t* blob = blobs + (size_t)blockIdx.x * kStateBytes;
+    const bool s = save != 0;
+    copy_part(blob + kStateRec, reinterpret_cast<uint8_t*>(v.rec + env), 128, s);
+    copy_part(blob + kStateRam, v.ram + (size_t)env * kRamBytes, kRamBytes, s);
+    copy_part(blob + kStatePrgRam, v.prg_ram + (size_t)env * kPrgRamBytes, kPrgRamBytes, s);
+    copy_part(blob + kStateNt, v.nt + (size_t)env * kNtBytes, kNtBytes, s);
+    copy_part(blob + kStatePal, v.pal + (size_t)env * kPalBytes, kPalBytes, s);
+    copy_part(blob + kStateOam, v.oam + (size_t)env * kOamBytes, kOamBytes, s);
+    copy_part(blob + kStateSnapNt, v.snap_nt + (size_t)env * kNtBytes, kNtBytes, s);
+    copy_part(blob + kStateSnapPal, v.snap_pal + (size_t)env * kPalBytes, kPalBytes, s);
+    copy_part(blob + kStateSnapOam, v.snap_oam + (size_t)env * kOamBytes, kOamBytes, s);
+    if (threadIdx.x == 0) {
+        float* f = reinterpret_cast<float*>(blob + kStateOut);
+        uint8_t* u = blob + kStateOut + 8;
+        if (s) {
+            f[0] = v.rewards[env];
+            f[1] = v.last_rewards[env];
+            u[0] = v.done[env];
+            u[1] = v.last_done[env];
+        } else {
+            v.rewards[env] = f[0];
+            v.last_rewards[env] = f[1];
+            v.done[env] = u[0];
+            v.last_done[env] = u[1];
+        }
+    }
+}
+
+// --------------------------------------------------------------------------
 // Resets.
 // --------------------------------------------------------------------------
 __global__ void reset_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ mask, uint32_t full) {
@@ -403,6 +450,12 @@ cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* a
 
 cudaError_t launch_reset(const BatchView* dv, uint32_t num_envs, const uint8_t* mask, bool full, cudaStream_t s) {
     reset_kernel<<<(num_envs + 127) / 128, 128, 0, s>>>(dv, mask, full ? 1u : 0u);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_state(const BatchView* dv, const uint32_t* envs, uint32_t count, uint8_t* blobs, bool save,
+                         cudaStream_t s) {
+    if (count) state_kernel<<<count, 128, 0, s>>>(dv, envs, blobs, save ? 1u : 0u);
     return cudaGetLastError();
 }
 

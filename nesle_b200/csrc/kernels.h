@@ -23,6 +23,9 @@ cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* a
                         uint32_t flags, uint32_t variant, uint32_t threads, cudaStream_t s,
                         unsigned long long* prof_op = nullptr, unsigned long long* prof_pc = nullptr);
 cudaError_t launch_reset(const BatchView* dv, uint32_t num_envs, const uint8_t* mask, bool full, cudaStream_t s);
+// envs: device array of `count` env indices; blobs: count x kStateBytes (device).
+cudaError_t launch_state(const BatchView* dv, const uint32_t* envs, uint32_t count, uint8_t* blobs, bool save,
+                         cudaStream_t s);
 cudaError_t launch_poke(const BatchView* dv, uint32_t num_envs, uint32_t address, uint32_t value, cudaStream_t s);
 cudaError_t launch_render(const BatchView* dv, uint32_t num_envs, uint8_t* out, int mode, cudaStream_t s);
 

@@ -83,6 +83,22 @@ typedef struct __attribute__((aligned(16))) BankRecord {
 static_assert(sizeof(BankRecord) == 48, "BankRecord layout");
 #endif
 
+// Saved env state (nesle_save_states / nesle_load_states): one flat blob per
+// env, every part 16-byte aligned.
+enum {
+    kStateRec = 0,                               // EnvRecord
+    kStateRam = kStateRec + 128,                 // 2048
+    kStatePrgRam = kStateRam + kRamBytes,        // 8192
+    kStateNt = kStatePrgRam + kPrgRamBytes,      // 2048
+    kStatePal = kStateNt + kNtBytes,             // 32
+    kStateOam = kStatePal + kPalBytes,           // 256
+    kStateSnapNt = kStateOam + kOamBytes,        // 2048
+    kStateSnapPal = kStateSnapNt + kNtBytes,     // 32
+    kStateSnapOam = kStateSnapPal + kPalBytes,   // 256
+    kStateOut = kStateSnapOam + kOamBytes,       // reward f32, last reward f32, done u8, last done u8, pad
+    kStateBytes = kStateOut + 16,                // 15,056
+};
+
 // Done predicates.
 enum {
     kDoneSmb = 0,         // reference predicate (cpp/include/nesle/cuda/batch_step.cuh:100-103)

@@ -33,6 +33,8 @@ from typing import Callable, Sequence
 
 import numpy as np
 
+from .fcs import Snapshot, write_fcs  # noqa: F401  (FCS writer; snapshots are a workload input)
+
 # ---------------------------------------------------------------------------
 # Counter-based RNG (SplitMix64 finaliser, Steele/Lea/Flood 2014).  The same
 # function is restated in C (oracle/nes_oracle.c) and CUDA (csrc/nes_core.cuh).
@@ -592,65 +594,6 @@ def sprite_scroll_rom(seed: int, *, blocks: int = 8, per_block: int = 16) -> Rom
         off = table + OPAQUE_TILE * 16
         chr_rom[off:off + 16] = b"\xff" * 16
     return RomInfo(ines_image(bytes(prg), bytes(chr_rom)), SPRITE_LOOP_HEAD, NMI_HANDLER, loop_bytes)
-
-
-# ---------------------------------------------------------------------------
-# FCEUX FCS save states (the snapshot input format of the reference binding,
-# cpp/include/nesle/fcs.hpp:187-226): 16-byte header "FCS\xff", then chunks
-# tag:u8 size:u32le payload, each payload a run of sub-chunks name[4] size:u32le.
-# ---------------------------------------------------------------------------
-
-
-@dataclass
-class Snapshot:
-    pc: int = 0
-    a: int = 0
-    x: int = 0
-    y: int = 0
-    sp: int = 0xFD
-    p: int = 0x24
-    cpu_ram: bytes = bytes(2048)
-    prg_ram: bytes = bytes(8192)
-    ppu_ctrl: int = 0
-    ppu_mask: int = 0
-    ppu_status: int = 0
-    ppu_oam_addr: int = 0
-    ppu_open_bus: int = 0
-    ppu_read_buffer: int = 0
-    ppu_x: int = 0
-    ppu_w: int = 0
-    ppu_v: int = 0
-    ppu_t: int = 0
-    nametable_ram: bytes = bytes(2048)
-    palette_ram: bytes = bytes(32)
-    oam: bytes = bytes(256)
-
-
-def _sub(name: str, payload: bytes) -> bytes:
-    return name.encode().ljust(4, b"\0") + struct.pack("<I", len(payload)) + payload
-
-
-def write_fcs(s: Snapshot) -> bytes:
-    cpu = b"".join([
-        _sub("PC", struct.pack("<H", s.pc)), _sub("A", bytes([s.a])), _sub("X", bytes([s.x])),
-        _sub("Y", bytes([s.y])), _sub("S", bytes([s.sp])), _sub("P", bytes([s.p])),
-        _sub("DB", b"\0"), _sub("RAM", s.cpu_ram),
-    ])
-    ppu = b"".join([
-        _sub("NTAR", s.nametable_ram), _sub("PRAM", s.palette_ram), _sub("SPRA", s.oam),
-        _sub("PPUR", bytes([s.ppu_ctrl, s.ppu_mask, s.ppu_status, 0])),
-        _sub("PSPL", bytes([s.ppu_oam_addr])), _sub("XOFF", bytes([s.ppu_x])),
-        _sub("VTGL", bytes([s.ppu_w])), _sub("RADD", struct.pack("<H", s.ppu_v)),
-        _sub("TADD", struct.pack("<H", s.ppu_t)), _sub("VBUF", bytes([s.ppu_read_buffer])),
-        _sub("PGEN", bytes([s.ppu_open_bus])),
-    ])
-    cart = _sub("WRAM", s.prg_ram)
-    header = b"FCS\xff" + bytes(12)
-
-    def chunk(tag: int, payload: bytes) -> bytes:
-        return bytes([tag]) + struct.pack("<I", len(payload)) + payload
-
-    return header + chunk(1, cpu) + chunk(3, ppu) + chunk(16, cart)
 
 
 def random_snapshot(seed: int, pc: int, *, nmi_and_rendering: bool = False) -> Snapshot:

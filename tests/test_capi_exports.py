@@ -68,3 +68,14 @@ def test_cpu_only_entry_points(lib_path):
     args, keep = _lib.make_create_args(4, 4, b"NES\x1a" + bytes(12))
     assert lib.nesle_create(ctypes.byref(args), ctypes.byref(h)) == _lib.NESLE_ERR_INVALID
     assert b"NROM" in lib.nesle_last_error()
+
+
+def test_state_blob_layout_matches_the_library(lib_path):
+    lib = _lib.load()
+    assert lib.nesle_state_bytes() == _lib.STATE_BYTES
+    end = 0
+    for name, (off, size) in _lib.STATE_PARTS.items():
+        assert off == end and off % 16 == 0, name  # consecutive, 16-byte aligned
+        end = off + size
+    assert end == _lib.STATE_BYTES and _lib.ENV_RECORD_DTYPE.itemsize == 128
+
