@@ -523,6 +523,11 @@ def main(argv=None) -> int:
     if args.envs is None:
         args.envs = 2048 if args.workload == "config5" else 65536
     rank, world, local = dist_env()
+    # Libraries (NCCL announces its version) may write to stdout; the result must
+    # be the only line there, so fd 1 points at stderr until it is printed.
+    result_out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     if args.impl == "reference":
         res = run_reference(args, rank, world, local)
     elif args.workload == "config5":
@@ -530,7 +535,7 @@ def main(argv=None) -> int:
     else:
         res = run_ours(args, rank, world, local)
     if res is not None:
-        print(json.dumps(res), flush=True)
+        print(json.dumps(res), file=result_out, flush=True)
     return 0
 
 
