@@ -499,7 +499,8 @@ def run_ppo(args, rank, world, local) -> dict | None:
                        "gamma": cfg.gamma, "gae_lambda": cfg.gae_lambda,
                        "policy": "bf16 MLP 2048->512->256 ReLU, 7 logits + value, random init",
                        "env": "config2 ROM and snapshot, 7-mask action table, RAM[$FF]==$FF done, fused auto-reset",
-                       "observation": "RAM via DLPack, no copy", "l2": "no flush (PPO step)",
+                       "observation": "RAM via DLPack, no copy",
+                       "l2": "no flush: each iteration writes 537 MB of rollout observations (> L2)",
                        "parallelism": f"env-sharded dp{world}, NCCL gradient all-reduce"},
             "roofline": step_roof,
             "update": {"ms": update_ms, "bound": "tensor", "achieved": tflops, "peak": bf16_peak,
