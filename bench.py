@@ -45,9 +45,6 @@ UNIT = "env-steps/s"
 # PPU scalars 88, controller/DMA/reward baselines 30, action 1, reward 4 +
 # done 1).
 BYTES_PER_ENV_STEP = 4476
-# Pixel mode adds the observation pass: presentation nametables 2048, palette 32
-# and OAM 256 read, the 84x84 observation 7056 written (13,868 B/env-step in all).
-BYTES_PER_OBS = 2048 + 32 + 256 + 7056
 
 
 def parse_args(argv=None):
@@ -58,6 +55,8 @@ def parse_args(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--envs", type=int, default=None, help="envs per GPU (65,536; 2,048 for config5)")
     ap.add_argument("--workload", default="config4", choices=["config4", "config3", "config2", "config1", "config5"])
+    ap.add_argument("--obs", default="gray84", choices=["gray84", "rgb", "index"],
+                    help="pixel mode (config3): the observation rendered every env-step")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args(argv)
@@ -82,14 +81,21 @@ def is_pixel(wl) -> bool:
     return wl.name.startswith("config3")
 
 
-def workload_config(wl, envs: int, world: int) -> dict:
+OBS_DESC = {"gray84": "gray 84x84 (7056 B/env) rendered every env-step from the palette-index frame",
+            "rgb": "RGB 240x256x3 (184,320 B/env) rendered every env-step (the reference render())",
+            "index": "palette-index frame 240x256 (61,440 B/env) rendered every env-step"}
+# Pixel-mode bytes per env-step of the observation pass: snapshot NT 2048 + palette 32 + OAM 256 read,
+# the observation written.
+OBS_WRITE = {"gray84": 7056, "rgb": 184320, "index": 61440}
+
+
+def workload_config(wl, envs: int, world: int, obs: str = "gray84") -> dict:
     return {
         "workload": f"{wl.name}: benchmark config {wl.name[6]}" if wl.name.startswith("config") else wl.name,
         "envs_per_gpu": envs,
         "total_envs": envs * world,
         "frameskip": wl.frameskip,
-        "observation": ("gray 84x84 (7056 B/env) rendered every env-step from the palette-index frame"
-                        if is_pixel(wl) else "ram (2048 B/env, zero-copy view)"),
+        "observation": (OBS_DESC[obs] if is_pixel(wl) else "ram (2048 B/env, zero-copy view)"),
         "snapshots": len(wl.snapshots),
         "done": {0: "smb", 1: "RAM[$FF]==$FF", 2: "frame limit U[500,5000]"}[wl.done_mode],
         "auto_reset": "fused",
@@ -294,10 +300,18 @@ def run_ours(args, rank, world, local) -> dict | None:
     def device_step(s):
         batch.step_device(acts[s], auto_reset=True, synchronize=False)
 
+    def render_obs():
+        if args.obs == "gray84":
+            batch.obs_gray84_device(render=True)
+        elif args.obs == "index":
+            batch.frames_index_device(render=True)
+        else:
+            batch.render_device()
+
     for s in range(args.warmup):
         device_step(s)
         if pixel:
-            batch.obs_gray84_device(render=True)
+            render_obs()
     torch.cuda.synchronize(dev)
     barrier()
     torch.cuda.synchronize(dev)
@@ -312,7 +326,7 @@ def run_ours(args, rank, world, local) -> dict | None:
             device_step(s)
             mids[i].record(stream)
             if pixel:
-                batch.obs_gray84_device(render=True)  # the observation of this env-step
+                render_obs()  # the observation of this env-step
             ends[i].record(stream)
         torch.cuda.synchronize(dev)
     barrier()
@@ -328,7 +342,7 @@ def run_ours(args, rank, world, local) -> dict | None:
         host_acts = torch.empty((total_steps, n), dtype=torch.uint8, pin_memory=True)
         host_acts.copy_(acts.cpu())
         host_np = host_acts.numpy()
-        obs_kw = dict(render_frame=False, copy_obs=True, obs_mode="gray84") if pixel else \
+        obs_kw = dict(render_frame=False, copy_obs=True, obs_mode=args.obs) if pixel else \
             dict(render_frame=False, copy_obs=False)
         for s in range(args.warmup):
             batch.step(host_np[s], **obs_kw)
@@ -361,7 +375,7 @@ def run_ours(args, rank, world, local) -> dict | None:
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-            "config": workload_config(wl, n, world),
+            "config": workload_config(wl, n, world, args.obs),
             "roofline": step_roof,
             "issue": {"emulated_instructions_per_s": instr / (kernel_ms / 1e3) if instr else None,
                       "emulated_instructions_per_env_step": instr / (n * world) if instr else None,
@@ -371,19 +385,21 @@ def run_ours(args, rank, world, local) -> dict | None:
             "clocks": clock_summary,
         }
         if pixel:
-            obs_roof = {"kernel": "gray84_kernel", "bound": "hbm",
-                        "achieved": BYTES_PER_OBS * n / (obs_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
-                        "traffic": profile_traffic("gray84_kernel_config3.txt"), "ms": obs_ms}
+            obs_bytes = 2048 + 32 + 256 + OBS_WRITE[args.obs]
+            obs_roof = {"kernel": "gray84_kernel" if args.obs == "gray84" else "render_kernel", "bound": "hbm",
+                        "achieved": obs_bytes * n / (obs_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                        "traffic": profile_traffic("gray84_kernel_config3.txt" if args.obs == "gray84"
+                                                   else f"render_kernel_{args.obs}_config3.txt"), "ms": obs_ms}
             obs_roof["frac"] = obs_roof["achieved"] / peak
             result["obs_kernel"] = obs_roof
             if obs_ms > kernel_ms:  # the roofline object describes the dominant kernel
                 result["roofline"], result["obs_kernel"] = obs_roof, step_roof
         if e2e_s:
-            d2h = (5 + (84 * 84 if pixel else 0)) * n * world
+            d2h = (5 + (OBS_WRITE[args.obs] if pixel else 0)) * n * world
             result["e2e"] = {"value": total_env_steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": n * world,
                              "d2h_bytes_per_step": d2h,
-                             "path": ("CudaBatch.step(pinned u8 actions, obs_mode='gray84') -> obs, rewards, dones "
-                                      "as numpy" if pixel else
+                             "path": (f"CudaBatch.step(pinned u8 actions, obs_mode='{args.obs}') -> obs, rewards, "
+                                      "dones as numpy" if pixel else
                                       "CudaBatch.step(pinned u8 actions) -> rewards, dones as numpy")}
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = reference_cpu_rate(wl, n, steps=2, warmup=1)
