@@ -168,44 +168,11 @@ NESLE_HD uint32_t lowest_set(uint64_t m) {
 // The view that paints row y's background (two-region split).
 NESLE_HD const RenderView& bg_view(const RenderEnv& e, uint32_t y) { return ((int)y < e.split) ? e.hud : e.lower; }
 
-// render_batch_rgb_pixel_env (:378-434) given the pixel's background colour
-// `bgc` (rv_background of bg_view), returning the colour index; `rows` is the
-// sprite_row_mask of scanline y (lowest index still wins).
-NESLE_HD uint32_t compose_pixel(const RenderEnv& e, uint32_t x, uint32_t y, uint32_t bgc, uint64_t rows) {
-    const RenderView& s = e.lower;
-    const bool lower_bg = (int)y >= e.split;
-    uint32_t c = bgc ? bgc : rv_palette(s, 0);
-    if ((s.mask & 0x10) && ((s.mask & 0x04) || x >= 8)) {
-        while (rows) {
-            const uint32_t i = lowest_set(rows);
-            rows &= rows - 1;
-            const uint8_t* so = s.oam + i * 4;
-            const int sy = (int)y - ((int)so[0] + 1);
-            const int sx = (int)x - (int)so[3];
-            if (sx < 0 || sx >= 8) continue;
-            const uint32_t attr = so[2];
-            if ((attr & 0x20) && (lower_bg ? bgc : rv_background(s, x, y)) != 0) continue;
-            const uint32_t sc = rv_sprite_px(s, so[1], attr, (uint32_t)sx, (uint32_t)sy);
-            if (sc == 0) continue;
-            c = rv_palette(s, 0x10 + (attr & 3) * 4 + sc);
-            break;
-        }
-    }
-    return c;
-}
-
-NESLE_HD uint32_t render_pixel_masked(const RenderEnv& e, uint32_t x, uint32_t y, uint64_t rows) {
-    return compose_pixel(e, x, y, rv_background(bg_view(e, y), x, y), rows);
-}
-
-NESLE_HD uint32_t render_pixel(const RenderEnv& e, uint32_t x, uint32_t y) {
-    return render_pixel_masked(e, x, y, sprite_row_mask(e, y));
-}
-
 // ---------------------------------------------------------------------------
-// Table-driven form of compose_pixel for the kernels (same result): the env's
-// 32 palette entries resolved once (`res[i]` = rv_palette(view, i); both views
-// share palette and mask), and one entry per sprite covering row y.
+// Pixel composition, render_batch_rgb_pixel_env (:378-434), from tables: the
+// env's 32 palette entries resolved once (`res[i]` = rv_palette(view, i); both
+// views share palette and mask), each sprite's pattern rows with flips applied,
+// and per-row tile entries of the background.
 // ---------------------------------------------------------------------------
 NESLE_HD void resolve_palette(const RenderEnv& e, uint8_t* res) {
     for (uint32_t i = 0; i < 32; ++i) res[i] = (uint8_t)rv_palette(e.lower, i);
@@ -224,9 +191,11 @@ NESLE_HD uint32_t sprite_pattern_row(const RenderView& s, uint32_t i, uint32_t r
     return lo | (hi << 8);
 }
 
-// compose_pixel from the tables; `spat[i * 16 + r]` is sprite_pattern_row(lower, i, r)
-// and `rows` any superset of the sprites covering pixel (x, y) (e.g. the row
-// mask ANDed with the column mask).
+// Colour index of pixel (x, y) given its background colour `bgc` (0 =
+// transparent, from bg_view): the lowest-index opaque sprite covering it wins,
+// a behind-background sprite only over transparent background.
+// `spat[i * 16 + r]` is sprite_pattern_row(lower, i, r) and `rows` any superset
+// of the sprites covering the pixel (the row mask ANDed with the column mask).
 NESLE_HD uint32_t compose_pixel_tables(const RenderEnv& e, const uint8_t* res, uint32_t x, uint32_t y, uint32_t bgc,
                                        uint64_t rows, const uint16_t* spat) {
     const RenderView& s = e.lower;
