@@ -276,9 +276,9 @@ static int create_impl(const nesle_create_args* a, nesle_batch* b) {
     // shared memory has the shorter one (B200, config-4 workload: 185k vs 77k
     // env-steps/s at 2,048 envs, 740k vs 592k at 16,384; in place wins from
     // 32,768 on).  Larger batches keep RAM in place, every env resident, with
-    // the zero page in shared memory (hybrid: config 4 at 65,536 envs 2.07 M vs
-    // 1.90 M all in place; configs 2 and 3 lose 3% and 7%).
-    // NESLE_STEP_KERNEL=shared|global|hybrid overrides.
+    // the zero page in shared memory (hybrid: config 4 at 65,536 envs 2.10 M vs
+    // 1.90 M all in place; config 2 loses 2%, config 3's step 7%).
+    // NESLE_STEP_KERNEL=shared|global|hybrid|hybrid-stack overrides.
     int sms = 0;
     CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, a->device), "SM count");
     b->step_variant = b->n <= 2u * (uint32_t)sms * kStepSlots ? kStepSharedRam : kStepHybridRam;
@@ -286,6 +286,7 @@ static int create_impl(const nesle_create_args* a, nesle_batch* b) {
         if (strcmp(sv, "global") == 0) b->step_variant = kStepGlobalRam;
         else if (strcmp(sv, "shared") == 0) b->step_variant = kStepSharedRam;
         else if (strcmp(sv, "hybrid") == 0) b->step_variant = kStepHybridRam;
+        else if (strcmp(sv, "hybrid-stack") == 0) b->step_variant = kStepHybridStackRam;
     }
     b->step_threads = global_step_threads(b->n, static_cast<uint32_t>(sms));
     CUDA_TRY(cudaEventCreateWithFlags(&b->done_event, cudaEventDisableTiming), "create event");
@@ -604,7 +605,8 @@ int nesle_get_info(nesle_batch* b, nesle_info* out) {
     out->device = static_cast<uint32_t>(b->device);
     out->envs_per_block = b->step_variant == kStepSharedRam ? kStepSlots : b->step_threads;
     out->smem_bytes_per_block = b->step_variant == kStepSharedRam ? static_cast<uint32_t>(step_smem_bytes())
-                                : 32768 + 16 + 256 * 32 + (b->step_variant == kStepHybridRam ? b->step_threads * 256 : 0);
+                                : 32768 + 16 + 256 * 32 +
+                                      (b->step_variant >= kStepHybridRam ? b->step_threads * 256 : 0);
     return NESLE_OK;
 }
 

@@ -70,6 +70,7 @@ step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
     c.slots = kStepSlots;
     c.zp = nullptr;
     c.zslots = 0;
+    c.zpage = 0;
     c.prg = s_prg;
     c.dec = s_dec;
     c.view = vp;
@@ -131,7 +132,7 @@ template <bool kProfile, bool kHybrid>
 __global__ void __launch_bounds__(kGlobalMaxThreads, 1)
 step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
                    const long long* __restrict__ act64, uint32_t flags, unsigned long long* __restrict__ prof_op,
-                   unsigned long long* __restrict__ prof_pc) {
+                   unsigned long long* __restrict__ prof_pc, uint32_t slot_page) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ uint32_t s_op[kProfile ? 256 : 1];
     uint8_t* s_prg = smem;
@@ -154,8 +155,9 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
         c.slots = 1;
         c.zp = nullptr;
         c.zslots = 0;
+        c.zpage = 0;
         if (kHybrid) {
-            const uint4* src = reinterpret_cast<const uint4*>(c.ram);
+            const uint4* src = reinterpret_cast<const uint4*>(c.ram + slot_page);
 #pragma unroll 4
             for (uint32_t q = 0; q < 16; ++q) {
                 const uint4 w = src[q];
@@ -166,6 +168,7 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
             }
             c.zp = reinterpret_cast<uint8_t*>(s_zp + tid);
             c.zslots = blockDim.x;
+            c.zpage = slot_page;
         }
         c.prg = s_prg;
         c.dec = s_dec;
@@ -186,7 +189,7 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
         if (kProfile) run_env_step<false>(c, rec, action, reward, done, DeviceProfile{s_op, prof_pc});
         else run_env_step<false>(c, rec, action, reward, done);
         if (kHybrid) {  // back in place before a possible auto-reset rewrites the row
-            uint4* dst = reinterpret_cast<uint4*>(c.ram);
+            uint4* dst = reinterpret_cast<uint4*>(c.ram + slot_page);
 #pragma unroll 4
             for (uint32_t q = 0; q < 16; ++q)
                 dst[q] = make_uint4(s_zp[(4 * q + 0) * blockDim.x + tid], s_zp[(4 * q + 1) * blockDim.x + tid],
@@ -432,15 +435,15 @@ cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* a
         if (!prof_op || !prof_pc) return cudaErrorInvalidValue;
         const uint32_t blocks = (num_envs + threads - 1) / threads;
         step_kernel_global<true, false><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags, prof_op,
-                                                                                    prof_pc);
+                                                                                    prof_pc, 0);
     } else if (variant == kStepGlobalRam) {
         const uint32_t blocks = (num_envs + threads - 1) / threads;
         step_kernel_global<false, false><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags, nullptr,
-                                                                                      nullptr);
-    } else if (variant == kStepHybridRam) {
+                                                                                      nullptr, 0);
+    } else if (variant == kStepHybridRam || variant == kStepHybridStackRam) {
         const uint32_t blocks = (num_envs + threads - 1) / threads;
         step_kernel_global<false, true><<<blocks, threads, kPrgSmem + kDecSmem + (size_t)threads * 256, s>>>(
-            dv, act8, act64, flags, nullptr, nullptr);
+            dv, act8, act64, flags, nullptr, nullptr, variant == kStepHybridStackRam ? 0x100u : 0u);
     } else {
         const uint32_t blocks = (num_envs + kStepSlots - 1) / kStepSlots;
         step_kernel<<<blocks, kStepSlots, step_smem_bytes(), s>>>(dv, act8, act64, flags);

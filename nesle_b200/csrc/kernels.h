@@ -11,7 +11,7 @@ namespace nesle {
 constexpr uint32_t kStepSlots = 64;       // envs (threads) per shared-RAM step CTA (multiple of 32: conflict-free banks)
 constexpr uint32_t kGlobalMaxThreads = 448;  // max envs (threads) per in-place step CTA
 
-enum : uint32_t { kStepSharedRam = 0, kStepGlobalRam = 1, kStepHybridRam = 2 };
+enum : uint32_t { kStepSharedRam = 0, kStepGlobalRam = 1, kStepHybridRam = 2, kStepHybridStackRam = 3 };
 
 enum : uint32_t { kStepDeviceApi = 1, kStepAutoReset = 2 };
 

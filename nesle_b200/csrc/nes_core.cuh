@@ -435,8 +435,9 @@ NESLE_HD void store_lane(const Lane& L, EnvRecord& r) {
 struct Ctx {
     uint8_t* ram;         // &smem_ram[slot * 4]; byte a at ram[(a & 0x7FC) * slots + (a & 3)]
     uint32_t slots;       // RAM slots per CTA (interleave stride / 4)
-    uint8_t* zp;          // hybrid placement: the env's zero-page slot in shared memory, else null
-    uint32_t zslots;      // lanes per zero-page row (interleave stride / 4)
+    uint8_t* zp;          // hybrid placement: the env's page slot in shared memory, else null
+    uint32_t zslots;      // lanes per slot row (interleave stride / 4)
+    uint32_t zpage;       // RAM page held in the slot: 0x000 (zero page) or 0x100 (stack)
     const uint8_t* prg;   // 32 KB (shared)
     const Entry* dec;     // execution entries (shared)
     const BatchView* view;
@@ -450,11 +451,11 @@ struct Ctx {
 };
 
 NESLE_HD uint32_t ram_off(const Ctx& c, uint32_t a) { return (a & 0x7FCu) * c.slots + (a & 3u); }
-// Byte `a` of the env's RAM.  With a zero-page slot (c.zp, hybrid placement)
-// $0000-$00FF and its mirrors live there, interleaved 4 bytes per lane with a
+// Byte `a` of the env's RAM.  With a page slot (c.zp, hybrid placement) the
+// page c.zpage and its mirrors live there, interleaved 4 bytes per lane with a
 // row of c.zslots lanes; everything else is at c.ram.
 NESLE_HD uint8_t* zp_slot(const Ctx& c, uint32_t a) { return c.zp + (a & 0xFCu) * c.zslots + (a & 3u); }
-NESLE_HD bool in_zp_slot(const Ctx& c, uint32_t a) { return c.zp && (a & 0x700u) == 0; }
+NESLE_HD bool in_zp_slot(const Ctx& c, uint32_t a) { return c.zp && (a & 0x700u) == c.zpage; }
 NESLE_HD uint8_t* ram_ptr(const Ctx& c, uint32_t a) {
     return in_zp_slot(c, a) ? zp_slot(c, a) : c.ram + ram_off(c, a);
 }
@@ -520,7 +521,7 @@ NESLE_HD void ppu_mem_wr(const Ctx& c, Lane& L, uint32_t a, uint32_t v) {
 // batch_bus.cuh:135-154: OAM DMA from RAM page & 0x7FF, +513 cycles.
 NESLE_HD void oam_dma(const Ctx& c, Lane& L, uint32_t page) {
     const uint32_t base = (page << 8) & 0x7FF;
-    if ((L.oam_addr & 0xFF) == 0 && !(c.zp && (base & 0x700u) == 0)) {
+    if ((L.oam_addr & 0xFF) == 0 && !(c.zp && (base & 0x700u) == c.zpage)) {
         // Aligned destination: assemble 4 RAM bytes (one interleaved smem word
         // each) and store 16 bytes at a time.
         for (uint32_t i = 0; i < 256; i += 16) {

@@ -129,6 +129,10 @@ class HostCoreHybrid(HostCore):
     global_ram = 2  # in place, zero page in a separate slot
 
 
+class HostCoreHybridStack(HostCore):
+    global_ram = 3  # in place, stack page in a separate slot
+
+
 class GpuCore(_Common):
     """libnesle_b200.so through its C ABI (host arrays in, host copies out)."""
 

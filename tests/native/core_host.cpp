@@ -32,7 +32,8 @@ struct HostBatch {
     std::vector<uint8_t> bram, bprg, bnt, bpal, boam, e2l;
     uint32_t fault = 0;
     bool global_ram = false;  // run the in-place (global-RAM) variant of the core
-    bool hybrid = false;      // ... with the zero page in a separate slot (hybrid placement)
+    bool hybrid = false;      // ... with one page in a separate slot (hybrid placement)
+    uint32_t slot_page = 0;   // the slot's page: 0x000 or 0x100
     std::vector<uint8_t> smem_ram = std::vector<uint8_t>(kSlots * kRamBytes);
 };
 
@@ -115,8 +116,9 @@ void host_destroy(void* p) { delete static_cast<HostBatch*>(p); }
 
 void host_set_global_ram(void* p, int on) {
     auto* h = static_cast<HostBatch*>(p);
-    h->global_ram = on != 0;  // 1 in place, 2 in place with the zero page in a separate slot
-    h->hybrid = on == 2;
+    h->global_ram = on != 0;  // 1 in place, 2 (3) in place with the zero page (stack page) in a separate slot
+    h->hybrid = on >= 2;
+    h->slot_page = on == 3 ? 0x100u : 0u;
 }
 
 void host_reset(void* p) {
@@ -167,9 +169,11 @@ void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) 
         c.oam = h->v.oam + (size_t)e * kOamBytes;
         c.zp = nullptr;
         c.zslots = 0;
-        uint32_t zp[64];  // hybrid placement: this env's zero page as one lane of words
+        c.zpage = 0;
+        uint32_t zp[64];  // hybrid placement: this env's slot page as one lane of words
         if (h->hybrid) {
-            memcpy(zp, h->ram.data() + (size_t)e * kRamBytes, 256);
+            c.zpage = h->slot_page;
+            memcpy(zp, h->ram.data() + (size_t)e * kRamBytes + c.zpage, 256);
             c.zp = reinterpret_cast<uint8_t*>(zp);
             c.zslots = 1;
         }
@@ -179,7 +183,7 @@ void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) 
         uint8_t done;
         if (h->global_ram) {
             run_env_step<false>(c, rec, actions[e], reward, done);
-            if (h->hybrid) memcpy(h->ram.data() + (size_t)e * kRamBytes, zp, 256);
+            if (h->hybrid) memcpy(h->ram.data() + (size_t)e * kRamBytes + c.zpage, zp, 256);
         } else {
             run_env_step<true>(c, rec, actions[e], reward, done);
             unstage(*h, e, slot);

@@ -6,7 +6,8 @@ import numpy as np
 import pytest
 
 import kat_roms as kat
-from harness import STATE_FIELDS, HostCore, HostCoreGlobal, HostCoreHybrid, assert_same, run_lockstep
+from harness import (STATE_FIELDS, HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreHybridStack, assert_same,
+                     run_lockstep)
 from nesle_b200 import workloads as w
 from oracle import Oracle
 
@@ -14,7 +15,7 @@ from oracle import Oracle
 @pytest.mark.parametrize("make,auto_reset", [(w.config1, False), (w.config2, True), (w.config3, True),
                                              (w.config4, True)])
 def test_configs_lockstep(make, auto_reset):
-    run_lockstep(make, 8, 8, auto_reset, [HostCore, HostCoreGlobal, HostCoreHybrid])
+    run_lockstep(make, 8, 8, auto_reset, [HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreHybridStack])
 
 
 def test_config3_frames_match_checker_every_step():
@@ -40,7 +41,7 @@ def test_frame_limit_auto_reset_lockstep():
         wl = w.config4()
         wl.done_args = (5, 17)
         return wl
-    _, _, dones = run_lockstep(short, 12, 20, True, [HostCore, HostCoreGlobal, HostCoreHybrid])
+    _, _, dones = run_lockstep(short, 12, 20, True, [HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreHybridStack])
     assert dones > 10
 
 
@@ -54,7 +55,7 @@ def test_smb_done_auto_reset_every_step():
     (kat.LDA_TAX_INX_STA, []), (kat.JSR_RTS, []), (kat.BNE_PAGE_CROSS, []), (kat.SEC_SBC, []),
     (kat.NMI_ROM, []), (kat.DMA_ROM, [kat.dma_snapshot()]), (kat.DMA_ZP_ROM, [kat.dma_zp_snapshot()]),
     (kat.IDLE_ROM, [])])
-@pytest.mark.parametrize("core", [HostCore, HostCoreGlobal, HostCoreHybrid])
+@pytest.mark.parametrize("core", [HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreHybridStack])
 def test_known_answer_roms(rom, snaps, core):
     o = Oracle(2, 2, rom, snaps)
     h = core(2, 2, rom, snaps)
@@ -99,7 +100,8 @@ def test_every_official_opcode_from_random_state(seed):
     """Each official opcode once from a random register/flag/RAM state (P bit 5 may be clear)."""
     for opc, rom, snap in _single_instruction_cases(seed, 1):
         o = Oracle(1, 1, rom, [snap])
-        sims = [HostCore(1, 1, rom, [snap]), HostCoreGlobal(1, 1, rom, [snap]), HostCoreHybrid(1, 1, rom, [snap])]
+        sims = [HostCore(1, 1, rom, [snap]), HostCoreGlobal(1, 1, rom, [snap]), HostCoreHybrid(1, 1, rom, [snap]),
+                HostCoreHybridStack(1, 1, rom, [snap])]
         a = np.zeros(1, np.uint8)
         o.step(a, auto_reset=False)
         for h in sims:

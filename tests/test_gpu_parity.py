@@ -29,7 +29,7 @@ def _cuda():
 
 @pytest.mark.parametrize("make,auto_reset,n", [(w.config1, False, 64), (w.config2, True, 200),
                                                (w.config3, True, 200), (w.config4, True, 200)])
-@pytest.mark.parametrize("variant", ["shared", "global", "hybrid"])
+@pytest.mark.parametrize("variant", ["shared", "global", "hybrid", "hybrid-stack"])
 def test_configs_lockstep(make, auto_reset, n, variant, monkeypatch):
     """Every step, every field, against the checker (200 envs = 2 full CTAs + a partial one),
     for both placements of env RAM in the step kernel."""
@@ -55,7 +55,7 @@ def test_frame_limit_auto_reset_many_episodes():
     (kat.LDA_TAX_INX_STA, []), (kat.JSR_RTS, []), (kat.BNE_PAGE_CROSS, []), (kat.SEC_SBC, []),
     (kat.NMI_ROM, []), (kat.DMA_ROM, [kat.dma_snapshot()]), (kat.DMA_ZP_ROM, [kat.dma_zp_snapshot()]),
     (kat.IDLE_ROM, [])])
-@pytest.mark.parametrize("variant", ["shared", "global", "hybrid"])
+@pytest.mark.parametrize("variant", ["shared", "global", "hybrid", "hybrid-stack"])
 def test_known_answer_roms(rom, snaps, variant, monkeypatch):
     monkeypatch.setenv("NESLE_STEP_KERNEL", variant)
     o = Oracle(3, 2, rom, snaps)
