@@ -122,7 +122,10 @@ typedef struct {
     uint32_t stat_frames, stat_budget_hits;
     uint8_t ram[2048], prg_ram[8192], nt[2048], pal[32], oam[256];
     uint8_t snap_oam[256], snap_nt[2048], snap_pal[32];
+    uint64_t ram_touch; /* MEASUREMENT: 32-byte RAM sectors read or written during the last env-step */
 } env_t;
+
+#define TOUCH(e, a) ((e)->ram_touch |= 1ull << (((a) & 0x7FFu) >> 5))
 
 typedef struct {
     uint16_t pc;
@@ -331,13 +334,16 @@ static uint8_t read_controller(env_t *e) {
 /* batch_bus.cuh:135-154 */
 static void oam_dma(env_t *e, uint8_t page) {
     uint16_t base = (uint16_t)(page << 8);
-    for (int i = 0; i < 256; ++i) e->oam[(uint8_t)(e->oam_addr + i)] = e->ram[(base + i) & 0x7FF];
+    for (int i = 0; i < 256; ++i) {
+        TOUCH(e, base + i);
+        e->oam[(uint8_t)(e->oam_addr + i)] = e->ram[(base + i) & 0x7FF];
+    }
     e->pending_dma += 513;
 }
 
 /* batch_bus.cuh:156-213 */
 static uint8_t bus_read(const nes_oracle *o, env_t *e, uint16_t a) {
-    if (a < 0x2000) return e->ram[a & 0x7FF];
+    if (a < 0x2000) { TOUCH(e, a); return e->ram[a & 0x7FF]; }
     if (a < 0x4000) {
         int reg = (a - 0x2000) & 7;
         if (reg == 2) {
@@ -378,7 +384,7 @@ static uint8_t bus_read(const nes_oracle *o, env_t *e, uint16_t a) {
 
 /* batch_bus.cuh:215-304 */
 static void bus_write(const nes_oracle *o, env_t *e, uint16_t a, uint8_t v) {
-    if (a < 0x2000) { e->ram[a & 0x7FF] = v; return; }
+    if (a < 0x2000) { TOUCH(e, a); e->ram[a & 0x7FF] = v; return; }
     if (a < 0x4000) {
         int reg = (a - 0x2000) & 7;
         if (reg == 0) {
@@ -707,6 +713,9 @@ static int bcd3(const uint8_t *ram, int a) {
 /* batch_step.cuh:51-106, plus the EXTENSION done predicates. */
 static void apply_reward(const nes_oracle *o, env_t *e, uint32_t env) {
     const uint8_t *ram = e->ram;
+    static const uint16_t kRead[] = {0x6D, 0x86, 0x7F8, 0x7F9, 0x7FA, 0x0E, 0xB5, 0x75A, 0x16, 0x1D, 0x770};
+    for (size_t i = 0; i < sizeof(kRead) / sizeof(kRead[0]); ++i) TOUCH(e, kRead[i]);
+    if (o->done_mode == ORACLE_DONE_RAM_EQ) TOUCH(e, o->done_a);
     int x = ram[0x6D] * 0x100 + ram[0x86];
     int time = bcd3(ram, 0x7F8);
     int dying = ram[0x0E] == 0x0B || ram[0xB5] > 1;
@@ -799,6 +808,7 @@ static void seed_presentation(env_t *e) {
  * fast-forward (batch_console.hpp:129-152) inlined.                            */
 /* ------------------------------------------------------------------------ */
 static void env_step(const nes_oracle *o, env_t *e, uint32_t env) {
+    e->ram_touch = 0;
     uint32_t pending = 0;
     uint32_t horizon = dots_to_next_event(e);
     uint64_t total_instr = 0;
@@ -1133,7 +1143,7 @@ static const field_t kFields[] = {
     FLD(done, 1), FLD(last_done, 1), FLD(action, 1), FLD(episode, 4), FLD(status, 4),
     FLD(stat_instructions, 8), FLD(stat_frames, 4), FLD(stat_budget_hits, 4),
     FLD(ram, 2048), FLD(prg_ram, 8192), FLD(nt, 2048), FLD(pal, 32), FLD(oam, 256),
-    FLD(snap_oam, 256), FLD(snap_nt, 2048), FLD(snap_pal, 32),
+    FLD(snap_oam, 256), FLD(snap_nt, 2048), FLD(snap_pal, 32), FLD(ram_touch, 8),
 };
 #undef FLD
 

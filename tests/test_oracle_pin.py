@@ -247,3 +247,24 @@ def test_reference_fcs_known_values():
     assert (d["pc"], d["a"], d["x"], d["y"], d["sp"], d["p"]) == (0x8057, 0x90, 0x00, 0x01, 0xFF, 0xA5)
     assert (d["ctrl"], d["mask"], d["status"], d["v"], d["t"]) == (0x90, 0x1E, 0x40, 0x0800, 0)
     assert (d["read_buffer"], d["open_bus"], d["pal"][0]) == (0xFF, 0x90, 0x22)
+
+
+def test_touched_ram_fraction_of_the_benchmark_workload():
+    """Config 4 (the metric's workload) touches >= 95% of each env's RAM sectors per
+    env-step, so its HBM bound is the full 4,476-B round trip; config 3 touches fewer."""
+    def fraction(make, steps=8, n=16):
+        wl = make()
+        env = np.arange(n)
+        e2l = wl.env_to_level(env) if wl.env_to_level else None
+        o = Oracle(n, 4, wl.rom.image, wl.snapshots, env_to_level=e2l, done_mode=wl.done_mode,
+                   done_args=wl.done_args, seed=wl.seed)
+        out = []
+        for s in range(steps):
+            o.step(wl.actions(env, s))
+            if s >= 2:
+                out += [bin(int(t)).count("1") / 64 for t in o.get("ram_touch")]
+        return float(np.mean(out))
+
+    assert fraction(w.config4) >= 0.95
+    assert fraction(w.config3) < 0.95
+
