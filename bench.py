@@ -52,7 +52,12 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-cuda"], default="ours",
+                    help="reference: the reference CPU core on the host cores; reference-cuda: the reference's "
+                         "own CUDA kernel (oracle/_ref/cuda, built by `make -C oracle ref-cuda`) on this GPU")
+    ap.add_argument("--done", choices=["workload", "smb"], default="workload",
+                    help="smb: the reference's SMB done predicate instead of the workload's (the only one the "
+                         "reference CUDA kernel has)")
     ap.add_argument("--envs", type=int, default=None, help="envs per GPU (65,536; 2,048 for config5)")
     ap.add_argument("--workload", default="config4", choices=["config4", "config3", "config2", "config1", "config5"])
     ap.add_argument("--obs", default="gray84", choices=["gray84", "rgb", "index"],
@@ -77,6 +82,14 @@ def make_workload(name: str):
             "config5": w.config2}[name]()
 
 
+def apply_done_option(wl, args):
+    if args.done == "smb":
+        from nesle_b200 import workloads as w
+
+        wl.done_mode, wl.done_args = w.DONE_SMB, (0, 0)
+    return wl
+
+
 def is_pixel(wl) -> bool:
     return wl.name.startswith("config3")
 
@@ -97,7 +110,7 @@ def workload_config(wl, envs: int, world: int, obs: str = "gray84") -> dict:
         "frameskip": wl.frameskip,
         "observation": (OBS_DESC[obs] if is_pixel(wl) else "ram (2048 B/env, zero-copy view)"),
         "snapshots": len(wl.snapshots),
-        "done": {0: "smb", 1: "RAM[$FF]==$FF", 2: "frame limit U[500,5000]"}[wl.done_mode],
+        "done": {0: "smb (reference predicate)", 1: "RAM[$FF]==$FF", 2: "frame limit U[500,5000]"}[wl.done_mode],
         "auto_reset": "fused",
         "actions": "uniform u8 joypad bytes (counter RNG)" if wl.name.startswith("config4") else "counter RNG",
         "l2": "state larger than L2 (RAM 128 MiB + records/OAM/PRG-RAM per 65,536 envs); no flush",
@@ -280,7 +293,7 @@ def run_ours(args, rank, world, local) -> dict | None:
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    wl = make_workload(args.workload)
+    wl = apply_done_option(make_workload(args.workload), args)
     n = args.envs
     offset, env = shard(rank, n)
     from nesle_b200.native_ppo import batch_snapshot_args
@@ -413,7 +426,7 @@ def run_reference(args, rank, world, local) -> dict | None:
     """The reference's CPU implementation of the path on this box's host cores."""
     if rank != 0:
         return None
-    wl = make_workload(args.workload)
+    wl = apply_done_option(make_workload(args.workload), args)
     base = reference_cpu_rate(wl, args.envs * world, steps=args.steps, warmup=args.warmup,
                               budget_s=min(120.0, 6.0 * (args.steps + args.warmup)))
     return {
@@ -424,6 +437,82 @@ def run_reference(args, rank, world, local) -> dict | None:
         "config": workload_config(wl, args.envs, world),
         "cpu_baseline": base,
         "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def load_reference_cuda():
+    """The reference's own pybind11 CUDA module, compiled unchanged for sm_100a."""
+    import importlib.util
+
+    found = sorted((ROOT / "oracle" / "_ref" / "cuda").glob("_cuda_core*.so"))
+    if not found:
+        return None
+    spec = importlib.util.spec_from_file_location("_cuda_core", found[0])
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def run_reference_cuda(args, rank, world, local) -> dict | None:
+    """The reference CUDA kernel (console_step_kernel through CudaBatch.step_device) on this GPU."""
+    if rank != 0:
+        return None
+    import torch
+
+    from nesle_b200 import build as nb
+    from nesle_b200 import workloads as w
+    from nesle_b200._cuda_core import CudaBatch
+    from nesle_b200.native_ppo import batch_snapshot_args
+
+    ref = load_reference_cuda()
+    if ref is None:
+        return {"impl": "reference-cuda", "unavailable": "reference CUDA binding not built (make -C oracle ref-cuda)"}
+    nb.build()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    wl = make_workload(args.workload)
+    wl.done_mode, wl.done_args = w.DONE_SMB, (0, 0)  # the reference kernel's only done predicate
+    n = args.envs
+    env = np.arange(n)
+    snap, e2l = batch_snapshot_args(wl, env)
+    total = args.warmup + args.steps
+    acts = torch.from_numpy(np.stack([wl.actions(env, s) for s in range(total)])).to(dev)
+    # Gate: the reference kernel executes `trap` on an illegal opcode.  Run this
+    # library's kernel (same semantics, but it records the opcode instead) on
+    # the identical inputs first; the reference runs only if none occurred.
+    ours = CudaBatch(n, wl.frameskip, wl.rom.image, snap, e2l, device=local, done_mode=w.DONE_SMB)
+    try:
+        for s in range(total):
+            ours.step_device(acts[s], auto_reset=True, synchronize=True)
+    except RuntimeError as exc:
+        return {"impl": "reference-cuda", "unavailable": f"illegal opcode on these inputs ({exc}); not run"}
+    del ours
+    if snap is None:
+        batch = ref.CudaBatch(n, wl.frameskip, wl.rom.image)
+    elif e2l is None:
+        batch = ref.CudaBatch(n, wl.frameskip, wl.rom.image, snap)
+    else:
+        batch = ref.CudaBatch(n, wl.frameskip, wl.rom.image, list(snap), e2l)
+    stream = torch.cuda.current_stream(dev)
+    for s in range(args.warmup):
+        batch.step_device(acts[s], auto_reset=True, synchronize=True)
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t0.record(stream)
+        for s in range(args.warmup, total):
+            batch.step_device(acts[s], auto_reset=True, synchronize=True)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    elapsed_ms = t0.elapsed_time(t1)
+    return {
+        "metric": METRIC, "value": n * args.steps / (elapsed_ms / 1e3), "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "impl": "reference-cuda",
+        "config": dict(workload_config(wl, n, 1), reference="cpp/bindings/cuda_module.cu + "
+                       "cpp/src/cuda/kernels.cu compiled unchanged for sm_100a; step_device(auto_reset=True)"),
+        "clocks": clocks.summary(),
     }
 
 
@@ -547,6 +636,8 @@ def main(argv=None) -> int:
     os.dup2(2, 1)
     if args.impl == "reference":
         res = run_reference(args, rank, world, local)
+    elif args.impl == "reference-cuda":
+        res = run_reference_cuda(args, rank, world, local)
     elif args.workload == "config5":
         res = run_ppo(args, rank, world, local)
     else:
