@@ -257,19 +257,30 @@ state_kernel(const BatchView* __restrict__ vp, const uint32_t* __restrict__ envs
 // --------------------------------------------------------------------------
 // Resets.
 // --------------------------------------------------------------------------
-__global__ void reset_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ mask, uint32_t full) {
+// One warp per env: lane 0 rewrites the record, the 32 lanes copy the byte
+// rows with contiguous 16-byte stores (512 bytes per warp store).
+__global__ void __launch_bounds__(128)
+reset_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ mask, uint32_t full) {
     const BatchView& v = *vp;
-    const uint32_t env = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t env = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (env >= v.num_envs) return;
-    if (!full && !mask[env]) return;
-    EnvRecord rec = v.rec[env];
-    if (full) rec.episode = 0;
-    else rec.episode++;
-    reset_env(v, env, rec);
-    v.rewards[env] = 0.0f;
-    v.done[env] = 0;
-    if (full) seed_presentation(v, env, rec);
-    v.rec[env] = rec;
+    if (!full && !mask[env]) return;  // both uniform across the warp
+    if (lane == 0) {
+        EnvRecord rec = v.rec[env];
+        if (full) rec.episode = 0;
+        else rec.episode++;
+        reset_record(v, env, rec);
+        if (full) seed_presentation_record(rec);
+        v.rec[env] = rec;
+        v.rewards[env] = 0.0f;
+        v.done[env] = 0;
+    }
+    reset_rows(v, env, lane, 32);
+    if (full) {
+        __syncwarp();  // the live rows are final before they are copied to the snapshot
+        seed_presentation_rows(v, env, lane, 32);
+    }
 }
 
 __global__ void poke_kernel(const BatchView* __restrict__ vp, uint32_t address, uint32_t value) {
@@ -452,7 +463,8 @@ cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* a
 }
 
 cudaError_t launch_reset(const BatchView* dv, uint32_t num_envs, const uint8_t* mask, bool full, cudaStream_t s) {
-    reset_kernel<<<(num_envs + 127) / 128, 128, 0, s>>>(dv, mask, full ? 1u : 0u);
+    const uint64_t threads = (uint64_t)num_envs * 32;  // a warp per env
+    reset_kernel<<<(uint32_t)((threads + 127) / 128), 128, 0, s>>>(dv, mask, full ? 1u : 0u);
     return cudaGetLastError();
 }
 

@@ -1093,7 +1093,17 @@ NESLE_HD void reward_done(const Ctx& c, Lane& L, float& reward, uint8_t& done) {
 // ---------------------------------------------------------------------------
 // Resets on global memory: batch_step.cuh:109-242.
 // ---------------------------------------------------------------------------
-NESLE_HD void cold_reset(const BatchView& v, uint32_t env, EnvRecord& r) {
+// Byte rows of resets, split over `lanes` cooperating threads (lane `lane`
+// takes every lanes-th 16-byte chunk); one thread passes (0, 1).
+NESLE_HD void zero_part(uint8_t* dst, uint32_t n, uint32_t lane, uint32_t lanes) {
+    for (uint32_t i = lane * 16; i < n; i += lanes * 16) store16(dst + i, 0, 0, 0, 0);
+}
+NESLE_HD void copy_part(uint8_t* dst, const uint8_t* src, uint32_t n, uint32_t lane, uint32_t lanes) {
+    for (uint32_t i = lane * 16; i < n; i += lanes * 16) copy16(dst + i, src + i);
+}
+
+// Record part of the power-on reset (batch_step.cuh:109-172).
+NESLE_HD void cold_reset_record(const BatchView& v, EnvRecord& r) {
     const uint32_t episode = r.episode;
     memset(&r, 0, sizeof(r));
     r.episode = episode;
@@ -1103,17 +1113,12 @@ NESLE_HD void cold_reset(const BatchView& v, uint32_t env, EnvRecord& r) {
     r.cycles = 7;
     r.ctrl_count = 8;
     r.flags = kFlagNtDirty | kFlagPalDirty | kFlagOamDirty;
-    const size_t e = env;
-    zero_row(v.ram + e * kRamBytes, kRamBytes);
-    zero_row(v.prg_ram + e * kPrgRamBytes, kPrgRamBytes);
-    zero_row(v.nt + e * kNtBytes, kNtBytes);
-    zero_row(v.pal + e * kPalBytes, kPalBytes);
-    zero_row(v.oam + e * kOamBytes, kOamBytes);
 }
 
-NESLE_HD void warm_reset(const BatchView& v, uint32_t env, EnvRecord& r) {
-    const uint32_t lvl = v.env_to_level[env];
-    const BankRecord& s = v.bank[lvl];
+// Record part of the snapshot reset from bank slot env_to_level[env]
+// (batch_step.cuh:174-242).
+NESLE_HD void warm_reset_record(const BatchView& v, uint32_t env, EnvRecord& r) {
+    const BankRecord& s = v.bank[v.env_to_level[env]];
     const uint32_t episode = r.episode;
     memset(&r, 0, sizeof(r));
     r.episode = episode;
@@ -1123,21 +1128,34 @@ NESLE_HD void warm_reset(const BatchView& v, uint32_t env, EnvRecord& r) {
     r.v = s.v; r.t = s.t; r.fine_x = s.fine_x; r.w = s.w; r.open_bus = s.open_bus; r.read_buffer = s.read_buffer;
     r.prev_x = s.prev_x; r.prev_time = s.prev_time;
     r.flags = kFlagNtDirty | kFlagPalDirty | kFlagOamDirty;
+}
+
+// Byte rows of the reset: zeroed (power-on) or copied from the bank slot.
+NESLE_HD void reset_rows(const BatchView& v, uint32_t env, uint32_t lane, uint32_t lanes) {
     const size_t e = env;
-    copy_row(v.ram + e * kRamBytes, v.bank_ram + (size_t)lvl * kRamBytes, kRamBytes);
-    copy_row(v.prg_ram + e * kPrgRamBytes, v.bank_prg_ram + (size_t)lvl * kPrgRamBytes, kPrgRamBytes);
-    copy_row(v.nt + e * kNtBytes, v.bank_nt + (size_t)lvl * kNtBytes, kNtBytes);
-    copy_row(v.pal + e * kPalBytes, v.bank_pal + (size_t)lvl * kPalBytes, kPalBytes);
-    copy_row(v.oam + e * kOamBytes, v.bank_oam + (size_t)lvl * kOamBytes, kOamBytes);
+    if (v.num_levels) {
+        const size_t lvl = v.env_to_level[env];
+        copy_part(v.ram + e * kRamBytes, v.bank_ram + lvl * kRamBytes, kRamBytes, lane, lanes);
+        copy_part(v.prg_ram + e * kPrgRamBytes, v.bank_prg_ram + lvl * kPrgRamBytes, kPrgRamBytes, lane, lanes);
+        copy_part(v.nt + e * kNtBytes, v.bank_nt + lvl * kNtBytes, kNtBytes, lane, lanes);
+        copy_part(v.pal + e * kPalBytes, v.bank_pal + lvl * kPalBytes, kPalBytes, lane, lanes);
+        copy_part(v.oam + e * kOamBytes, v.bank_oam + lvl * kOamBytes, kOamBytes, lane, lanes);
+    } else {
+        zero_part(v.ram + e * kRamBytes, kRamBytes, lane, lanes);
+        zero_part(v.prg_ram + e * kPrgRamBytes, kPrgRamBytes, lane, lanes);
+        zero_part(v.nt + e * kNtBytes, kNtBytes, lane, lanes);
+        zero_part(v.pal + e * kPalBytes, kPalBytes, lane, lanes);
+        zero_part(v.oam + e * kOamBytes, kOamBytes, lane, lanes);
+    }
 }
 
 // The reset kernels of the reference rewrite the console state only: the
 // presentation-snapshot scalars and the per-step statistics of the step that
 // triggered the reset survive.
-NESLE_HD void reset_env(const BatchView& v, uint32_t env, EnvRecord& r) {
+NESLE_HD void reset_record(const BatchView& v, uint32_t env, EnvRecord& r) {
     const EnvRecord keep = r;
-    if (v.num_levels) warm_reset(v, env, r);
-    else cold_reset(v, env, r);
+    if (v.num_levels) warm_reset_record(v, env, r);
+    else cold_reset_record(v, r);
     r.lat_sx = keep.lat_sx; r.lat_sy = keep.lat_sy; r.lat_ctrl = keep.lat_ctrl;
     r.snap_sx_start = keep.snap_sx_start; r.snap_sy_start = keep.snap_sy_start;
     r.snap_ctrl_start = keep.snap_ctrl_start; r.snap_sx_end = keep.snap_sx_end;
@@ -1147,17 +1165,30 @@ NESLE_HD void reset_env(const BatchView& v, uint32_t env, EnvRecord& r) {
     r.stat_budget_hits = keep.stat_budget_hits;
 }
 
-// cuda_module.cu:1443-1463: presentation snapshot from live state.
-NESLE_HD void seed_presentation(const BatchView& v, uint32_t env, EnvRecord& r) {
-    const size_t e = env;
-    copy_row(v.snap_nt + e * kNtBytes, v.nt + e * kNtBytes, kNtBytes);
-    copy_row(v.snap_pal + e * kPalBytes, v.pal + e * kPalBytes, kPalBytes);
-    copy_row(v.snap_oam + e * kOamBytes, v.oam + e * kOamBytes, kOamBytes);
+// Snapshot (warm) or power-on (cold) reset of one env by one thread.
+NESLE_HD void reset_env(const BatchView& v, uint32_t env, EnvRecord& r) {
+    reset_record(v, env, r);
+    reset_rows(v, env, 0, 1);
+}
+
+// cuda_module.cu:1443-1463: presentation snapshot from live state -- the
+// record part, then the rows (after the live rows are final).
+NESLE_HD void seed_presentation_record(EnvRecord& r) {
     r.snap_mask = r.ppu_mask;
     r.lat_sx = r.snap_sx_start = r.snap_sx_end = r.scroll_x;
     r.lat_sy = r.snap_sy_start = r.snap_sy_end = r.scroll_y;
     r.lat_ctrl = r.snap_ctrl_start = r.snap_ctrl_end = r.ppu_ctrl;
     r.flags &= ~(uint8_t)(kFlagNtDirty | kFlagPalDirty | kFlagOamDirty);
+}
+NESLE_HD void seed_presentation_rows(const BatchView& v, uint32_t env, uint32_t lane, uint32_t lanes) {
+    const size_t e = env;
+    copy_part(v.snap_nt + e * kNtBytes, v.nt + e * kNtBytes, kNtBytes, lane, lanes);
+    copy_part(v.snap_pal + e * kPalBytes, v.pal + e * kPalBytes, kPalBytes, lane, lanes);
+    copy_part(v.snap_oam + e * kOamBytes, v.oam + e * kOamBytes, kOamBytes, lane, lanes);
+}
+NESLE_HD void seed_presentation(const BatchView& v, uint32_t env, EnvRecord& r) {
+    seed_presentation_rows(v, env, 0, 1);
+    seed_presentation_record(r);
 }
 
 // ---------------------------------------------------------------------------
