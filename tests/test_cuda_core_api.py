@@ -250,3 +250,47 @@ def test_step_profile_histograms_match_checker(torch, make):
         b.step_device(torch.from_numpy(wl.actions(env, 10 + s)).cuda())  # unprofiled steps in between
         o.step(wl.actions(env, 10 + s))
 
+
+
+@pytest.mark.gpu
+def test_views_keep_the_batch_alive(torch):
+    """The lifetime contract of the reference views (cuda_module.cu keep_alive<0, 1>,
+    tests/test_env_reset_state.py): a view -- and a tensor made from it -- keeps its
+    CudaBatch alive.  Checked by weak reference; freed memory is never touched."""
+    import gc
+    import weakref
+
+    b, wl, env = _batch(8)
+    ref = weakref.ref(b)
+    view = b.ram_device()
+    t = torch.utils.dlpack.from_dlpack(b.rewards_device())
+    del b
+    gc.collect()
+    assert ref() is not None  # held by `view` and by `t`
+    del view
+    gc.collect()
+    assert ref() is not None  # still held through the DLPack tensor
+    assert t.shape == (8,)
+    del t
+    gc.collect()
+    assert ref() is None
+
+
+@pytest.mark.gpu
+def test_render_after_step_matches_inline_render(torch):
+    """tests/test_render_freshness.py: step(render_frame=False) + render() and
+    step(render_frame=True) give the same, fresh frame."""
+    wl = w.config3()
+    n = 4
+    from nesle_b200._cuda_core import CudaBatch
+
+    a = CudaBatch(n, 4, wl.rom.image, device=0)
+    c = CudaBatch(n, 4, wl.rom.image, device=0)
+    first = a.render()
+    acts = np.full(n, 0x80, np.uint8)
+    for _ in range(6):
+        a.step(acts, render_frame=False, copy_obs=False)
+        out = c.step(acts, render_frame=True, copy_obs=True)
+    fa = a.render()
+    np.testing.assert_array_equal(fa, out["obs"])
+    assert int((fa != first).sum()) > 100  # the frame moved on
