@@ -68,7 +68,7 @@ def make_model(obs_dim: int, action_dim: int, hidden_sizes: tuple[int, int], dev
             nn.init.zeros_(self.critic.bias)
 
         def forward(self, obs):
-            with torch.autocast("cuda", dtype=torch.bfloat16, enabled=obs.is_cuda):
+            with torch.autocast("cuda", dtype=torch.bfloat16, enabled=obs.is_cuda, cache_enabled=False):
                 x = obs.to(torch.bfloat16 if obs.is_cuda else torch.float32) * (1.0 / 255.0)
                 f = self.net(x)
                 logits, value = self.actor(f), self.critic(f).squeeze(-1)
@@ -130,7 +130,7 @@ class PPOTrainer:
     """One process (one GPU) of the GPU-resident PPO loop on a CudaBatch."""
 
     def __init__(self, config: NativePPOConfig, workload: w.Workload | None = None, *, device: int = 0,
-                 rank: int = 0, world: int = 1):
+                 rank: int = 0, world: int = 1, use_graphs: bool = True):
         import torch
 
         from ._cuda_core import CudaBatch
@@ -159,7 +159,13 @@ class PPOTrainer:
 
             for p in self.model.parameters():
                 dist.broadcast(p.data, src=0)
-        self.opt = torch.optim.Adam(self.model.parameters(), lr=config.learning_rate, eps=1e-5)
+        # CUDA-graph the minibatch update on one GPU (capturable Adam keeps its
+        # step counters on the device)
+        self.use_graphs = world == 1 and use_graphs
+        self._graph = None
+        self._eager_steps = 0
+        self.opt = torch.optim.Adam(self.model.parameters(), lr=config.learning_rate, eps=1e-5,
+                                    capturable=self.use_graphs)
         T, N = config.n_steps, config.num_envs
         self.obs_buf = torch.empty((T, N, 2048), dtype=torch.uint8, device=self.dev)
         self.act_buf = torch.empty((T, N), dtype=torch.long, device=self.dev)
@@ -194,8 +200,67 @@ class PPOTrainer:
             self.next_done.copy_(self.dones)
         self.global_step += self.cfg.num_envs * self.cfg.n_steps * self.world
 
+    def _minibatch_loss(self, obs, act, logp, adv, ret):
+        """Clipped-surrogate PPO loss of one minibatch (native_ppo.py:545-563)."""
+        import torch
+
+        cfg = self.cfg
+        logits, newvalue = self.model(obs)
+        logp_all = torch.log_softmax(logits, dim=-1)
+        newlogp = logp_all.gather(1, act[:, None]).squeeze(1)
+        entropy = -(logp_all.exp() * logp_all).sum(-1).mean()
+        ratio = (newlogp - logp).exp()
+        mb_adv = (adv - adv.mean()) / (adv.std() + 1e-8)
+        pg_loss = torch.max(-mb_adv * ratio,
+                            -mb_adv * torch.clamp(ratio, 1.0 - cfg.clip_coef, 1.0 + cfg.clip_coef)).mean()
+        v_loss = 0.5 * (newvalue - ret).pow(2).mean()
+        return pg_loss - cfg.ent_coef * entropy + cfg.vf_coef * v_loss
+
+    def _eager_step(self, obs, act, logp, adv, ret):
+        import torch
+
+        params = list(self.model.parameters())
+        loss = self._minibatch_loss(obs, act, logp, adv, ret)
+        self.opt.zero_grad(set_to_none=True)
+        loss.backward()
+        allreduce_mean_grads(params, self.world)
+        torch.nn.utils.clip_grad_norm_(params, self.cfg.max_grad_norm)
+        self.opt.step()
+        return loss.detach()
+
+    def _graph_step(self, b, idx):
+        """One minibatch update as a CUDA graph replay (single GPU): the minibatch
+        is gathered into static buffers, then forward, backward, clipping and the
+        Adam step replay from one captured graph."""
+        import torch
+
+        g = self._graph
+        for name, src in zip(("obs", "act", "logp", "adv", "ret"), b):
+            torch.index_select(src, 0, idx, out=g[name])
+        g["graph"].replay()
+        return g["loss"].detach().clone()
+
+    def _capture(self, b, idx):
+        import torch
+
+        params = list(self.model.parameters())
+        static = {name: torch.index_select(src, 0, idx)
+                  for name, src in zip(("obs", "act", "logp", "adv", "ret"), b)}
+        graph = torch.cuda.CUDAGraph()
+        self.opt.zero_grad(set_to_none=True)
+        with torch.cuda.graph(graph):
+            loss = self._minibatch_loss(static["obs"], static["act"], static["logp"], static["adv"], static["ret"])
+            loss.backward()
+            torch.nn.utils.clip_grad_norm_(params, self.cfg.max_grad_norm)
+            self.opt.step()
+        static["loss"] = loss
+        static["graph"] = graph
+        self._graph = static
+
     def update(self) -> dict[str, Any]:
-        """GAE + update_epochs passes of clipped-surrogate minibatch updates."""
+        """GAE + update_epochs passes of clipped-surrogate minibatch updates.
+        On one GPU the minibatch step replays a captured CUDA graph after a few
+        eager warm-up steps; across GPUs it stays eager (NCCL all-reduce)."""
         import torch
 
         cfg = self.cfg
@@ -203,35 +268,25 @@ class PPOTrainer:
             _, next_value = self.model(self.obs)
             adv, ret = compute_gae(self.rew_buf, self.done_buf, self.val_buf, self.next_done, next_value,
                                    cfg.gamma, cfg.gae_lambda)
-        b_obs = self.obs_buf.reshape(-1, 2048)
-        b_act = self.act_buf.reshape(-1)
-        b_logp = self.logp_buf.reshape(-1)
-        b_adv = adv.reshape(-1)
-        b_ret = ret.reshape(-1)
-        count = b_obs.shape[0]
-        params = list(self.model.parameters())
+        b = (self.obs_buf.reshape(-1, 2048), self.act_buf.reshape(-1), self.logp_buf.reshape(-1),
+             adv.reshape(-1), ret.reshape(-1))
+        count = b[0].shape[0]
         losses = []
         for _ in range(cfg.update_epochs):
             perm = torch.randperm(count, device=self.dev)
             for start in range(0, count, cfg.batch_size):
                 idx = perm[start:start + cfg.batch_size]
-                logits, newvalue = self.model(b_obs[idx])
-                logp_all = torch.log_softmax(logits, dim=-1)
-                newlogp = logp_all.gather(1, b_act[idx][:, None]).squeeze(1)
-                entropy = -(logp_all.exp() * logp_all).sum(-1).mean()
-                ratio = (newlogp - b_logp[idx]).exp()
-                mb_adv = b_adv[idx]
-                mb_adv = (mb_adv - mb_adv.mean()) / (mb_adv.std() + 1e-8)
-                pg_loss = torch.max(-mb_adv * ratio,
-                                    -mb_adv * torch.clamp(ratio, 1.0 - cfg.clip_coef, 1.0 + cfg.clip_coef)).mean()
-                v_loss = 0.5 * (newvalue - b_ret[idx]).pow(2).mean()
-                loss = pg_loss - cfg.ent_coef * entropy + cfg.vf_coef * v_loss
-                self.opt.zero_grad(set_to_none=True)
-                loss.backward()
-                allreduce_mean_grads(params, self.world)
-                torch.nn.utils.clip_grad_norm_(params, cfg.max_grad_norm)
-                self.opt.step()
-                losses.append(loss.detach())
+                full = idx.shape[0] == cfg.batch_size  # a trailing partial minibatch steps eagerly
+                if full and self._graph is not None:
+                    losses.append(self._graph_step(b, idx))
+                    continue
+                if full and self.use_graphs and self._eager_steps >= 3:
+                    torch.cuda.synchronize(self.dev)
+                    self._capture(b, idx)
+                    losses.append(self._graph_step(b, idx))
+                    continue
+                losses.append(self._eager_step(*(x[idx] for x in b)))
+                self._eager_steps += 1
         return {"loss": torch.stack(losses).mean(), "samples": count}
 
     def iteration(self) -> dict[str, Any]:

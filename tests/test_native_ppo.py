@@ -115,3 +115,29 @@ def test_training_runs_and_env_side_replays_on_checker():
         assert np.isfinite(float(stats["loss"]))
     np.testing.assert_array_equal(tr.batch.ram(), o.get("ram"))
     assert len(np.unique(tr.act_buf.cpu().numpy())) > 1  # the policy samples several actions
+
+
+@pytest.mark.gpu
+def test_graphed_update_matches_eager_update():
+    """The single-GPU CUDA-graph update replays the eager minibatch step."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from nesle_b200 import build
+    from nesle_b200.native_ppo import NativePPOConfig, PPOTrainer
+
+    build.build()
+    cfg = NativePPOConfig(num_envs=64, n_steps=16, batch_size=128, update_epochs=2)
+    out = []
+    for graphs in (False, True):
+        tr = PPOTrainer(cfg, use_graphs=graphs)  # reseeds: identical init and rollout
+        tr.rollout()
+        stats = tr.update()
+        out.append((tr.obs_buf.cpu(), float(stats["loss"]), [p.detach().cpu() for p in tr.model.parameters()],
+                    tr._graph is not None))
+    (obs_e, loss_e, par_e, g_e), (obs_g, loss_g, par_g, g_g) = out
+    assert not g_e and g_g  # the second trainer really replayed a graph
+    assert torch.equal(obs_e, obs_g)
+    # float tolerance: bf16 autocast, and Adam's capturable and eager formulas round differently
+    assert abs(loss_e - loss_g) <= 1e-3 * max(1.0, abs(loss_e))
+    for a, b in zip(par_e, par_g):
+        torch.testing.assert_close(a, b, rtol=1e-3, atol=5e-4)
