@@ -77,6 +77,16 @@ struct nesle_batch {
         *out = static_cast<T*>(p);
         return NESLE_OK;
     }
+    // Frees one allocation made by alloc() (a no-op for null).
+    void free_one(void* p) {
+        if (!p) return;
+        for (size_t i = 0; i < allocations.size(); ++i)
+            if (allocations[i] == p) {
+                cudaFree(p);
+                allocations.erase(allocations.begin() + (long)i);
+                return;
+            }
+    }
     void release() {
         for (void* p : allocations) cudaFree(p);
         allocations.clear();
@@ -431,7 +441,13 @@ static int state_io(nesle_batch* b, const uint32_t* envs, uint32_t count, int en
                 return fail(NESLE_ERR_INVALID, "env index " + std::to_string(envs[i]) + " out of range (batch of " +
                                                    std::to_string(b->n) + ")");
     if ((!envs_on_device || !blobs_on_device) && count > b->state_cap) {
-        // staging grows to the largest request (one allocation per growth, freed with the batch)
+        // staging grows to the largest request; the outgrown pair is freed
+        CUDA_TRY(cudaStreamSynchronize(s), "state staging synchronize");
+        b->free_one(b->d_state_envs);
+        b->free_one(b->d_state_blobs);
+        b->d_state_envs = nullptr;
+        b->d_state_blobs = nullptr;
+        b->state_cap = 0;
         TRY(b->alloc(&b->d_state_envs, count, "state env list"));
         TRY(b->alloc(&b->d_state_blobs, (size_t)count * kStateBytes, "state blobs"));
         b->state_cap = count;
