@@ -12,6 +12,7 @@ import pytest
 
 import kat_roms as kat
 from harness import STATE_FIELDS, GpuCore, assert_same, run_lockstep
+from nesle_b200 import _lib
 from nesle_b200 import workloads as w
 from oracle import Oracle
 
@@ -213,3 +214,53 @@ def test_full_size_properties():
         g.step(wl.actions(np.arange(65536), s))
     np.testing.assert_array_equal(g.get("ram"), a["ram"])
     np.testing.assert_array_equal(g.get("cycles"), a["cycles"])
+
+
+def _windows_match(wl, full, offsets, n, steps, fields, render=False):
+    """Re-run envs [off, off+n) on the checker and compare with rows of a full-size GPU run."""
+    for off in offsets:
+        env = np.arange(off, off + n)
+        e2l = wl.env_to_level(env) if wl.env_to_level else None
+        o = Oracle(n, wl.frameskip, wl.rom.image, wl.snapshots, env_to_level=e2l, done_mode=wl.done_mode,
+                   done_args=wl.done_args, seed=wl.seed, env_offset=off)
+        for s in range(steps):
+            o.step(wl.actions(env, s))
+        for f in fields:
+            np.testing.assert_array_equal(o.get(f), full[f][off:off + n], err_msg=f"{f} at envs {off}+")
+        if render:
+            np.testing.assert_array_equal(o.render()["gray84"], full["gray84"][off:off + n],
+                                          err_msg=f"gray84 at envs {off}+")
+
+
+def _full_run(wl, n, steps):
+    env = np.arange(n)
+    e2l = wl.env_to_level(env) if wl.env_to_level else None
+    g = GpuCore(n, wl.frameskip, wl.rom.image, wl.snapshots, env_to_level=e2l, done_mode=wl.done_mode,
+                done_args=wl.done_args, seed=wl.seed)
+    for s in range(steps):
+        g.step(wl.actions(env, s))
+    return g
+
+
+def test_ragged_multiwave_batch_matches_checker():
+    """150,001 envs (hybrid placement, several waves of CTAs, a partial last CTA):
+    windows at the start, the middle and the end re-run on the checker."""
+    wl = w.config4()
+    n = 150_001
+    g = _full_run(wl, n, 2)
+    fields = ("pc", "a", "x", "y", "sp", "p", "cycles", "ram", "last_reward", "last_done")
+    full = {f: g.get(f) for f in fields + ("status",)}
+    assert (full["status"] == 0).all()
+    _windows_match(wl, full, [0, 75_000 - 40, n - 64], 64, 2, fields)
+
+
+def test_full_size_pixel_mode_matches_checker():
+    """Config 3 at 65,536 envs: state and 84x84 observations of three windows."""
+    wl = w.config3()
+    n = 65536
+    g = _full_run(wl, n, 2)
+    fields = ("pc", "ram", "oam", "scroll_x", "last_done")
+    full = {f: g.get(f) for f in fields}
+    _lib.check(g.lib.nesle_render(g._h, _lib.RENDER_GRAY84, None))
+    full["gray84"] = g.get("obs_gray84")
+    _windows_match(wl, full, [0, 32_768 - 16, n - 32], 32, 2, fields, render=True)
