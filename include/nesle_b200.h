@@ -121,7 +121,9 @@ int nesle_render_gray84_noalloc(nesle_batch* b, uint8_t* host_out, uint64_t byte
  * (NESLE_ERR_INVALID), device indices past the batch are skipped.  With host
  * blobs the call synchronises; with device blobs it is asynchronous on
  * `stream`.  The blob layout is this library's and can change with
- * nesle_abi_version(). */
+ * nesle_abi_version().  Loaded blobs are taken as saved: a hand-edited
+ * controller state outside what the bus can produce (count > 8, or shift bits
+ * at or above bit 8 - count) is normalised by the next step. */
 uint64_t nesle_state_bytes(void);
 int nesle_save_states(nesle_batch* b, const uint32_t* envs, uint32_t count, int envs_on_device, void* dst,
                       int dst_on_device, void* stream);

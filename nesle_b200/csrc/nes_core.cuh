@@ -373,6 +373,15 @@ NESLE_HD uint32_t frame_limit(const BatchView& v, uint32_t env, uint32_t episode
     return v.done_a + (uint32_t)(k % (uint64_t)(v.done_b - v.done_a + 1));
 }
 
+// Index of the highest set bit (v != 0).
+NESLE_HD uint32_t msb_index(uint32_t v) {
+#if defined(__CUDA_ARCH__)
+    return 31u - (uint32_t)__clz(v);
+#else
+    return 31u - (uint32_t)__builtin_clz(v);
+#endif
+}
+
 // ---------------------------------------------------------------------------
 // Lane state: every scalar of the env, register-resident during a launch.
 // ---------------------------------------------------------------------------
@@ -383,7 +392,7 @@ struct Lane {
     uint32_t frame_dot, ctrl, mask, status, nmi;
     uint32_t oam_addr, v, t, fine_x, w, open_bus, read_buffer, scroll_x, scroll_y;
     uint32_t lat_sx, lat_sy, lat_ctrl, ssx0, ssy0, sc0, ssx1, ssy1, sc1, smask;
-    uint32_t cshift, ccount, cstrobe, action, flags;
+    uint32_t csr, cstrobe, action, flags;  // csr: controller shift register, marker form (load_lane)
     int32_t prev_x, prev_time;
     uint32_t episode, status_word, cpu_nmi, irq;
     uint32_t dma;  // pending OAM-DMA cycles of the current instruction
@@ -403,8 +412,15 @@ NESLE_HD void load_lane(Lane& L, const EnvRecord& r, uint8_t action) {
     L.lat_sx = r.lat_sx; L.lat_sy = r.lat_sy; L.lat_ctrl = r.lat_ctrl;
     L.ssx0 = r.snap_sx_start; L.ssy0 = r.snap_sy_start; L.sc0 = r.snap_ctrl_start;
     L.ssx1 = r.snap_sx_end; L.ssy1 = r.snap_sy_end; L.sc1 = r.snap_ctrl_end; L.smask = r.snap_mask;
-    L.cshift = r.ctrl_shift; L.ccount = r.ctrl_count; L.cstrobe = r.ctrl_strobe; L.flags = r.flags;
-    L.action = action;
+    // Controller shift register as one value: the unread bits under a marker
+    // bit, so a read is `csr & 1` then `csr >>= 1` while csr > 1, and csr == 1
+    // means all 8 bits are read (further reads return 1).  Exact for every state
+    // the bus can reach (count <= 8, shift < 2^(8 - count)).  `action` carries
+    // the marker for a latch.
+    const uint32_t cnt = r.ctrl_count < 8 ? r.ctrl_count : 8u;
+    L.csr = (r.ctrl_shift & ((0x100u >> cnt) - 1u)) | (0x100u >> cnt);
+    L.cstrobe = r.ctrl_strobe; L.flags = r.flags;
+    L.action = (uint32_t)action | 0x100u;
     L.prev_x = r.prev_x; L.prev_time = r.prev_time; L.episode = r.episode; L.status_word = r.status;
     L.cpu_nmi = r.cpu_nmi_pending; L.irq = r.irq_pending; L.dma = r.pending_dma;
 }
@@ -421,7 +437,9 @@ NESLE_HD void store_lane(const Lane& L, EnvRecord& r) {
     r.snap_sx_start = (uint8_t)L.ssx0; r.snap_sy_start = (uint8_t)L.ssy0; r.snap_ctrl_start = (uint8_t)L.sc0;
     r.snap_sx_end = (uint8_t)L.ssx1; r.snap_sy_end = (uint8_t)L.ssy1; r.snap_ctrl_end = (uint8_t)L.sc1;
     r.snap_mask = (uint8_t)L.smask;
-    r.ctrl_shift = (uint8_t)L.cshift; r.ctrl_count = (uint8_t)L.ccount; r.ctrl_strobe = (uint8_t)L.cstrobe;
+    const uint32_t top = msb_index(L.csr);
+    r.ctrl_shift = (uint8_t)(L.csr ^ (1u << top)); r.ctrl_count = (uint8_t)(8u - top);
+    r.ctrl_strobe = (uint8_t)L.cstrobe;
     r.flags = (uint8_t)L.flags; r.prev_x = L.prev_x; r.prev_time = L.prev_time;
     r.pending_dma = L.dma; r.episode = L.episode; r.status = L.status_word;
     r.cpu_nmi_pending = (uint8_t)L.cpu_nmi; r.irq_pending = (uint8_t)L.irq;
@@ -573,12 +591,8 @@ NESLE_HD uint32_t io_rd(const Ctx& c, Lane& L, uint32_t a) {
     }
     if (a == 0x4016) {  // batch_bus.cuh:110-123
         if (L.cstrobe) return 0x40 | (L.action & 1);
-        uint32_t bit = 1;
-        if (L.ccount < 8) {
-            bit = L.cshift & 1;
-            L.cshift >>= 1;
-            L.ccount++;
-        }
+        const uint32_t bit = L.csr & 1;
+        if (L.csr > 1) L.csr >>= 1;
         return 0x40 | bit;
     }
     if (a == 0x4017) return 0x41;
@@ -636,7 +650,7 @@ NESLE_HD void io_wr(const Ctx& c, Lane& L, uint32_t a, uint32_t val) {
     if (a == 0x4014) { oam_dma(c, L, val); return; }
     if (a == 0x4016) {  // batch_bus.cuh:125-133
         const uint32_t next = val & 1;
-        if (next || L.cstrobe) { L.cshift = L.action; L.ccount = 0; }
+        if (next || L.cstrobe) L.csr = L.action;
         L.cstrobe = next;
         return;
     }
@@ -884,7 +898,7 @@ NESLE_HD uint32_t exec_uniform(const Ctx& c, Lane& L, Fetched& f, bool& fresh) {
         mem = c.prg[addr & 0x7FFF];
         if (rd && is_ram) mem = *ram_byte;
     }
-    const uint32_t cbit = L.cstrobe ? (L.action & 1u) : (L.ccount < 8 ? (L.cshift & 1u) : 1u);
+    const uint32_t cbit = (L.cstrobe ? L.action : L.csr) & 1u;
     uint32_t m = (is_ram || is_prg) ? mem : (is_ctrl ? (0x40u | cbit) : (addr == 0x4017u ? 0x41u : 0u));
     m = (w0 & E0_IMM) ? b1 : m;
     const bool io_space = (addr - 0x2000u < 0x2000u) || (addr - 0x6000u < 0x2000u);
@@ -893,9 +907,8 @@ NESLE_HD uint32_t exec_uniform(const Ctx& c, Lane& L, Fetched& f, bool& fresh) {
         m = io_rd(c, L, addr);
         side = true;
     }
-    const bool shift_now = rd && is_ctrl && !L.cstrobe && L.ccount < 8;  // batch_bus.cuh:115-121
-    L.cshift = shift_now ? (L.cshift >> 1) : L.cshift;
-    L.ccount += shift_now ? 1u : 0u;
+    const bool shift_now = rd && is_ctrl && !L.cstrobe && L.csr > 1u;  // batch_bus.cuh:115-121
+    L.csr = shift_now ? (L.csr >> 1) : L.csr;
 
     // ---- ALU: operands and units merged through the entry's masks ----
     const uint32_t opa = ((R >> byte_of(w1, 3)) & byte_of(w2, 0)) | (m & byte_of(w2, 1)) |
@@ -922,8 +935,7 @@ NESLE_HD uint32_t exec_uniform(const Ctx& c, Lane& L, Fetched& f, bool& fresh) {
     if (wm && is_ram) *ram_byte = (uint8_t)r;
     const bool cw = wm && is_ctrl;  // $4016 strobe (batch_bus.cuh:125-133)
     const bool latch = cw && ((r & 1u) || L.cstrobe);
-    L.cshift = latch ? L.action : L.cshift;
-    L.ccount = latch ? 0u : L.ccount;
+    L.csr = latch ? L.action : L.csr;
     L.cstrobe = cw ? (r & 1u) : L.cstrobe;
     if (wm && (io_space || addr == 0x4014u)) {
         io_wr(c, L, addr, r);
@@ -1051,7 +1063,10 @@ NESLE_HD void run_frames(const Ctx& c, Lane& L, const Prof& prof = Prof()) {
         L.cycles += it_cyc;
         L.pending += it_cyc * 3u;
         L.instr++;
-        if (op == 0x4C && L.pc == pc && L.fcomp == 0) {
+        // JMP to itself.  The reference also requires that no frame completed
+        // in this iteration; that always holds here, because a completed frame
+        // sends the next iteration through loop_top before any instruction runs.
+        if (op == 0x4C && L.pc == pc) {
             idle_fast_forward(c, L);
             fresh = false;
         }
