@@ -4,7 +4,7 @@
 //   step_kernel     one env-step per thread, env RAM staged in shared memory
 //   reset_kernel    masked or full snapshot/cold reset
 //   poke_kernel     one RAM byte in every env
-//   render_kernel   colour index or RGB per pixel from the presentation snapshot
+//   render_kernel   colour-index or RGB frame from the presentation snapshot
 //   gray84_kernel   84x84 area-resampled luma observation
 #include <cuda_runtime.h>
 #include <stdlib.h>
@@ -332,81 +332,218 @@ __device__ __forceinline__ RenderEnv stage_snapshot(const BatchView& v, uint32_t
     return e;
 }
 
-// Per strip of 20 rows: the background tile entries of each row.
-struct StripSmem {
-    uint32_t tiles[kGrayStripRows][kRowTiles];
-};
-
-// One strip of 20 rows: the tile entries (built by the whole CTA), then one
-// pixel per thread from its row's entries and the sprite tables.
-__device__ __forceinline__ void build_strip(const RenderEnv& e, uint32_t row0, StripSmem& st) {
-    for (uint32_t i = threadIdx.x; i < kGrayStripRows * kRowTiles; i += blockDim.x) {
-        const uint32_t r = i / kRowTiles, j = i % kRowTiles, y = row0 + r;
-        st.tiles[r][j] = slot_entry(bg_view(e, y), y, j);
+// Resident CTAs per SM the render kernels are compiled for (register caps of
+// 40 and 48): both are issue-bound with a barrier per phase, so occupancy
+// pays; 6 and 5 measured best (gray84 is limited to 5 by shared memory).
+constexpr int kRenderMinBlocks = 6, kGrayMinBlocks = 5;
+// Sprite-free pixels of one 8-column segment: row y, columns 8 c8 .. 8 c8 + 7,
+// packed one per byte (pixel p in byte p % 4 of out[p / 4]).  `tiles` are the
+// row's tile entries (slot j = scrolled tile column (sx >> 3) + j); a pixel is
+// the byte of its palette group's word `group` picked by its pattern value
+// (colours or luma, see group_colors).  Returns the sprites that may cover the
+// segment (0: the values are final).
+__device__ __forceinline__ uint64_t segment_background(const RenderEnv& e, const SnapSmem& sm, const uint32_t* tiles,
+                                                       const uint32_t* group, uint32_t y, uint32_t c8,
+                                                       uint32_t out[2]) {
+    const RenderView& bv = bg_view(e, y);
+    const RenderView& s = e.lower;
+    uint32_t lo8 = 0, hi8 = 0, grp0 = 0, grp1 = 0, keep = 8;  // pixels p < keep are in tile slot c8
+    if ((bv.mask & 0x08) && ((bv.mask & 0x02) || c8 != 0)) {
+        const uint32_t e0 = tiles[c8], e1 = tiles[c8 + 1], fine = bv.sx & 7u;
+        lo8 = ((((e0 & 0xFFu) << 8) | (e1 & 0xFFu)) << fine >> 8) & 0xFFu;  // pixel p at bit 7 - p
+        hi8 = (((e0 & 0xFF00u) | ((e1 >> 8) & 0xFFu)) << fine >> 8) & 0xFFu;
+        grp0 = (e0 >> 16) & 3u;
+        grp1 = (e1 >> 16) & 3u;
+        keep = 8u - fine;
     }
-}
-__device__ __forceinline__ uint32_t strip_pixel(const RenderEnv& e, const SnapSmem& sm, const StripSmem& st,
-                                                uint32_t row0, uint32_t x, uint32_t y) {
-    const RenderView& v = bg_view(e, y);
-    const uint32_t bgc = bg_from_entry_tables(v, sm.res, st.tiles[y - row0][tile_slot(v, x)], x, v.sx + x);
-    return compose_pixel_tables(e, sm.res, x, y, bgc, sm.rows[y] & sm.cols[x >> 3], sm.spat);
+    const uint32_t w0 = group[grp0], w1 = group[grp1];
+    out[0] = out[1] = 0u;
+#pragma unroll
+    for (uint32_t p = 0; p < 8; ++p) {
+        const uint32_t col = ((lo8 >> (7 - p)) & 1u) | (((hi8 >> (7 - p)) & 1u) << 1);
+        out[p >> 2] |= __byte_perm(p < keep ? w0 : w1, 0u, 0x4440u | col) << (8 * (p & 3));
+    }
+    return ((s.mask & 0x10) && ((s.mask & 0x04) || c8 != 0)) ? (sm.rows[y] & sm.cols[c8]) : 0ull;
 }
 
-__global__ void __launch_bounds__(kRenderThreads)
+// What a sprite-free pixel of palette group g shows for pattern value 0..3, as
+// bytes: the backdrop for 0, else colour 4g+c -- or the backdrop again when
+// that colour is index 0, which the reference composes as transparent
+// (compose_pixel_tables' `bgc ? bgc : res[0]`).
+__device__ __forceinline__ uint32_t group_colors(const SnapSmem& sm, uint32_t grp) {
+    uint32_t w = sm.res[0];
+    for (uint32_t c = 1; c < 4; ++c) {
+        const uint32_t col = sm.res[grp * 4 + c];
+        w |= (col ? col : (uint32_t)sm.res[0]) << (8 * c);
+    }
+    return w;
+}
+
+// Colour index of pixel (x, y) with the sprites `spr` that may cover it.
+__device__ __forceinline__ uint32_t sprite_pixel(const RenderEnv& e, const SnapSmem& sm, const uint32_t* tiles,
+                                                 uint32_t x, uint32_t y, uint64_t spr) {
+    const RenderView& bv = bg_view(e, y);
+    const uint32_t bgc = bg_from_entry_tables(bv, sm.res, tiles[tile_slot(bv, x)], x, bv.sx + x);
+    return compose_pixel_tables(e, sm.res, x, y, bgc, spr, sm.spat);
+}
+
+// One strip of `rows` rows into `buf` (row r at buf + r * 256): tile entries,
+// then (A) every 8-column segment from the tile entries, listing the segments
+// a sprite may cover, then (B) those segments' pixels one per thread, composed
+// with the sprites.  kLuma stores luma (lut[colour]) instead of colours.
+// Ends with a barrier; `list` holds rows * 32 entries.
+template <bool kLuma>
+__device__ __forceinline__ void render_strip(const RenderEnv& e, const SnapSmem& sm, uint32_t* tiles, uint32_t row0,
+                                             uint32_t rows, const uint32_t* group, const uint8_t* lut, uint8_t* buf,
+                                             uint16_t* list, uint32_t& count) {
+    const uint32_t tid = threadIdx.x, lane = tid & 31u;
+    for (uint32_t i = tid; i < rows * kRowTiles; i += blockDim.x) {
+        const uint32_t r = i / kRowTiles, j = i - r * kRowTiles, y = row0 + r;
+        tiles[i] = slot_entry(bg_view(e, y), y, j);
+    }
+    if (tid == 0) count = 0;
+    __syncthreads();
+    for (uint32_t sg = tid; sg < rows * 32u; sg += blockDim.x) {  // whole warps: rows * 32 is a warp multiple
+        const uint32_t r = sg >> 5, c8 = sg & 31u;
+        uint32_t w[2];
+        const uint64_t spr = segment_background(e, sm, tiles + r * kRowTiles, group, row0 + r, c8, w);
+        *reinterpret_cast<uint2*>(buf + r * kFrameW + 8u * c8) = make_uint2(w[0], w[1]);
+        const uint32_t want = __ballot_sync(__activemask(), spr != 0);
+        if (want) {
+            const uint32_t first = __ffs(want) - 1u;
+            uint32_t base = 0;
+            if (lane == first) base = atomicAdd(&count, (uint32_t)__popc(want));
+            base = __shfl_sync(__activemask(), base, first);
+            if (spr) list[base + __popc(want & ((1u << lane) - 1u))] = (uint16_t)sg;
+        }
+    }
+    __syncthreads();
+    const uint32_t tasks = count * 8u;
+    for (uint32_t t = tid; t < tasks; t += blockDim.x) {
+        const uint32_t sg = list[t >> 3], r = sg >> 5, c8 = sg & 31u, x = 8u * c8 + (t & 7u), y = row0 + r;
+        const uint32_t c = sprite_pixel(e, sm, tiles + r * kRowTiles, x, y, sm.rows[y] & sm.cols[c8]);
+        buf[r * kFrameW + x] = (uint8_t)(kLuma ? lut[c] : c);
+    }
+    __syncthreads();
+}
+
+// Colour-index or RGB frame, one CTA per env, strips of 20 rows rendered into
+// shared memory (render_strip), then written out as 8-byte (index) or 3 x
+// 8-byte (RGB) stores, each warp covering a contiguous stretch of the frame.
+constexpr uint32_t kRenderStripRows = 20;
+__global__ void __launch_bounds__(kRenderThreads, kRenderMinBlocks)
 render_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint32_t rgb) {
     __shared__ __align__(16) SnapSmem sm;
-    __shared__ StripSmem st;
+    __shared__ uint32_t s_tiles[kRenderStripRows * kRowTiles];
+    __shared__ __align__(16) uint8_t s_buf[kRenderStripRows * kFrameW];
+    __shared__ uint16_t s_list[kRenderStripRows * 32];
+    __shared__ uint32_t s_rgb[64];
+    __shared__ uint32_t s_group[4];
+    __shared__ uint32_t s_count;
     const BatchView& v = *vp;
-    const uint32_t env = blockIdx.x;
+    const uint32_t env = blockIdx.x, tid = threadIdx.x;
+    if (tid < 64)
+        s_rgb[tid] = kPaletteRgb[tid * 3] | ((uint32_t)kPaletteRgb[tid * 3 + 1] << 8) |
+                     ((uint32_t)kPaletteRgb[tid * 3 + 2] << 16);
     const RenderEnv e = stage_snapshot(v, env, sm);
+    if (tid < 4) s_group[tid] = group_colors(sm, tid);  // read after render_strip's first barrier
     uint8_t* dst = out + (size_t)env * (kFrameW * kFrameH) * (rgb ? 3u : 1u);
-    for (uint32_t row0 = 0; row0 < kFrameH; row0 += kGrayStripRows) {
-        build_strip(e, row0, st);
-        __syncthreads();
-        for (uint32_t p = threadIdx.x; p < kGrayStripRows * kFrameW; p += kRenderThreads) {
-            const uint32_t y = row0 + p / kFrameW, x = p % kFrameW;
-            const uint32_t c = strip_pixel(e, sm, st, row0, x, y);
-            const size_t q = (size_t)y * kFrameW + x;
+    for (uint32_t row0 = 0; row0 < kFrameH; row0 += kRenderStripRows) {
+        render_strip<false>(e, sm, s_tiles, row0, kRenderStripRows, s_group, nullptr, s_buf, s_list, s_count);
+        uint8_t* d = dst + (size_t)row0 * kFrameW * (rgb ? 3u : 1u);
+        for (uint32_t q = tid; q < kRenderStripRows * kFrameW / 8u; q += kRenderThreads) {
+            const uint2 w = *reinterpret_cast<const uint2*>(s_buf + 8u * q);
             if (rgb) {
-                dst[q * 3 + 0] = kPaletteRgb[c * 3 + 0];
-                dst[q * 3 + 1] = kPaletteRgb[c * 3 + 1];
-                dst[q * 3 + 2] = kPaletteRgb[c * 3 + 2];
+                uint32_t b[6];  // 8 pixels x 3 bytes
+#pragma unroll
+                for (uint32_t p = 0; p < 8; ++p) {
+                    const uint32_t c = s_rgb[(((p < 4) ? w.x : w.y) >> (8 * (p & 3))) & 0x3Fu];
+#pragma unroll
+                    for (uint32_t ch = 0; ch < 3; ++ch) {
+                        const uint32_t o = 3 * p + ch;
+                        if (o % 4 == 0) b[o / 4] = 0;
+                        b[o / 4] |= ((c >> (8 * ch)) & 0xFFu) << (8 * (o % 4));
+                    }
+                }
+                uint2* o = reinterpret_cast<uint2*>(d + 24u * q);
+                o[0] = make_uint2(b[0], b[1]);
+                o[1] = make_uint2(b[2], b[3]);
+                o[2] = make_uint2(b[4], b[5]);
             } else {
-                dst[q] = (uint8_t)c;
+                *reinterpret_cast<uint2*>(d + 8u * q) = w;
             }
         }
-        __syncthreads();
+        __syncthreads();  // s_buf is rewritten by the next strip
     }
 }
 
-// 84x84 grey observation, one CTA per env, on the same staged snapshot.  The
-// frame is done in 12 strips of 20 source rows: every source pixel is rendered
-// once into a shared luma strip, from which the strip's 7 x 84 outputs are
-// area-summed (gray84_pixel).  Nothing but the 7,056-byte observation is written.
-__global__ void __launch_bounds__(kRenderThreads)
+// 84x84 grey observation, one CTA per env, on the same staged snapshot, in 6
+// strips of 40 source rows (exactly 14 output rows each):
+//   1. the strip as luma (render_strip with the palette groups in luma);
+//   2. horizontal area sums: output column ox covers source columns
+//      64 ox / 21 .. + 3 with weights in units of 1/21 px;
+//   3. vertical area sums over 3-4 rows (1/7 px units), rounded: the integer
+//      (sum(luma * wx * wy) + 640) / 1280 of gray84_pixel, as a separable sum.
+// Nothing but the 7,056-byte observation is written to global memory.
+constexpr uint32_t kG84Rows = 40, kG84Out = 14;
+static_assert(kFrameH % kG84Rows == 0 && kG84Rows * kGray == kG84Out * kFrameH, "strip geometry");
+
+struct Gray84Smem {
+    uint32_t tiles[kG84Rows * kRowTiles];
+    __align__(16) uint8_t luma[kG84Rows * kFrameW];
+    uint16_t h[kG84Rows + 1][kGray];  // + a zero row read with weight 0
+    uint16_t list[kG84Rows * 32];
+    uint32_t hx[kGray];               // first source column | 4 weights x 5 bits from bit 8
+    uint32_t vy[kG84Out];             // first strip row | 4 weights x 5 bits from bit 8
+    uint32_t group_luma[4];           // luma version of group_colors
+    uint32_t count;
+    uint8_t lut[64];                  // luma of each NES colour
+};
+
+__device__ __forceinline__ uint32_t span_weights(uint32_t first, uint32_t unit, uint32_t lo, uint32_t hi) {
+    uint32_t w = first;
+    for (uint32_t j = 0; j < 4; ++j) {
+        const uint32_t a = (first + j) * unit, b = a + unit;
+        const uint32_t x = umin(b, hi) > umax(a, lo) ? umin(b, hi) - umax(a, lo) : 0u;
+        w |= x << (8 + 5 * j);
+    }
+    return w;
+}
+
+__global__ void __launch_bounds__(kRenderThreads, kGrayMinBlocks)
 gray84_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out) {
     __shared__ __align__(16) SnapSmem sm;
-    __shared__ StripSmem st;
-    __shared__ __align__(16) uint8_t s_luma[kGrayStripRows * kFrameW];
-    __shared__ uint8_t s_lut[64];
+    __shared__ Gray84Smem g;
     const BatchView& v = *vp;
     const uint32_t env = blockIdx.x, tid = threadIdx.x;
-    if (tid < 64) s_lut[tid] = (uint8_t)luma_of_rgb(kPaletteRgb[tid * 3], kPaletteRgb[tid * 3 + 1], kPaletteRgb[tid * 3 + 2]);
-    const RenderEnv e = stage_snapshot(v, env, sm);  // its barriers also cover s_lut
-
+    if (tid < 64) g.lut[tid] = (uint8_t)luma_of_rgb(kPaletteRgb[tid * 3], kPaletteRgb[tid * 3 + 1], kPaletteRgb[tid * 3 + 2]);
+    if (tid < kGray) {
+        g.hx[tid] = span_weights(64u * tid / 21u, 21u, 64u * tid, 64u * tid + 64u);
+        g.h[kG84Rows][tid] = 0;
+    }
+    if (tid < kG84Out) g.vy[tid] = span_weights(20u * tid / 7u, 7u, 20u * tid, 20u * tid + 20u);
+    const RenderEnv e = stage_snapshot(v, env, sm);  // its barriers also cover the tables above
+    if (tid < 4) {  // read after render_strip's first barrier
+        const uint32_t w = group_colors(sm, tid);
+        uint32_t l = 0;
+        for (uint32_t b = 0; b < 4; ++b) l |= (uint32_t)g.lut[(w >> (8 * b)) & 0xFFu] << (8 * b);
+        g.group_luma[tid] = l;
+    }
     uint8_t* dst = out + (size_t)env * kGray * kGray;
-    for (uint32_t k = 0; k < kFrameH / kGrayStripRows; ++k) {
-        const uint32_t row0 = k * kGrayStripRows;
-        build_strip(e, row0, st);
-        __syncthreads();
-        for (uint32_t p = tid; p < kGrayStripRows * kFrameW; p += kRenderThreads) {
-            const uint32_t y = row0 + p / kFrameW, x = p % kFrameW;
-            s_luma[p] = s_lut[strip_pixel(e, sm, st, row0, x, y)];
+    for (uint32_t k = 0; k < kFrameH / kG84Rows; ++k) {
+        render_strip<true>(e, sm, g.tiles, k * kG84Rows, kG84Rows, g.group_luma, g.lut, g.luma, g.list, g.count);
+        for (uint32_t i = tid; i < kG84Rows * kGray; i += kRenderThreads) {
+            const uint32_t r = i / kGray, ox = i - r * kGray, w = g.hx[ox];
+            const uint8_t* l = &g.luma[r * kFrameW + (w & 0xFFu)];
+            g.h[r][ox] = (uint16_t)(l[0] * ((w >> 8) & 31u) + l[1] * ((w >> 13) & 31u) + l[2] * ((w >> 18) & 31u) +
+                                    l[3] * ((w >> 23) & 31u));
         }
         __syncthreads();
-        for (uint32_t o = tid; o < kGrayStripOut * kGray; o += kRenderThreads) {
-            const uint32_t oy = k * kGrayStripOut + o / kGray, ox = o % kGray;
-            dst[oy * kGray + ox] = (uint8_t)gray84_pixel(s_luma, row0, ox, oy);
+        for (uint32_t i = tid; i < kG84Out * kGray; i += kRenderThreads) {
+            const uint32_t oyl = i / kGray, ox = i - oyl * kGray, w = g.vy[oyl], r = w & 0xFFu;
+            const uint32_t acc = g.h[r][ox] * ((w >> 8) & 31u) + g.h[r + 1][ox] * ((w >> 13) & 31u) +
+                                 g.h[r + 2][ox] * ((w >> 18) & 31u) + g.h[r + 3][ox] * ((w >> 23) & 31u);
+            dst[(k * kG84Out + oyl) * kGray + ox] = (uint8_t)((acc + 640u) / 1280u);
         }
         __syncthreads();
     }

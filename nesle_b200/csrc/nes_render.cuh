@@ -38,9 +38,15 @@ struct RenderView {
     uint32_t sx, sy, ctrl, mask;
 };
 
+// CHR byte at pattern address a (< $2000): CHR mirrored over its size, 0
+// without CHR ROM.  Power-of-two sizes (8 KB for NROM) skip the division.
+NESLE_HD uint32_t rv_chr(const RenderView& v, uint32_t a) {
+    if (!v.chr_size) return 0u;
+    return v.chr[(v.chr_size & (v.chr_size - 1u)) ? a % v.chr_size : a & (v.chr_size - 1u)];
+}
 NESLE_HD uint32_t rv_mem(const RenderView& v, uint32_t a) {  // batch_render.cuh:104-121
     a &= 0x3FFF;
-    if (a < 0x2000) return v.chr_size ? v.chr[a % v.chr_size] : 0u;
+    if (a < 0x2000) return rv_chr(v, a);
     if (a < 0x3F00) {
         if (a >= 0x3000) a -= 0x1000;
         return v.nt[mirror_nt(v.horizontal, a)];
@@ -178,15 +184,35 @@ NESLE_HD void resolve_palette(const RenderEnv& e, uint8_t* res) {
     for (uint32_t i = 0; i < 32; ++i) res[i] = (uint8_t)rv_palette(e.lower, i);
 }
 
+NESLE_HD uint32_t reverse8(uint32_t b) {
+#if defined(__CUDA_ARCH__)
+    return __brev(b) >> 24;
+#else
+    b = ((b & 0xF0u) >> 4) | ((b & 0x0Fu) << 4);
+    b = ((b & 0xCCu) >> 2) | ((b & 0x33u) << 2);
+    return ((b & 0xAAu) >> 1) | ((b & 0x55u) << 1);
+#endif
+}
+
 // Row r (0..15) of sprite i with any flips applied: pixel sx of the row at
-// bit sx of the low (bits 0-7) and high (bits 8-15) plane.
+// bit sx of the low (bits 0-7) and high (bits 8-15) plane.  Same pixels as
+// rv_sprite_px over sx = 0..7: one pattern byte pair, reversed unless the
+// sprite is flipped horizontally (pattern pixel p sits at bit 7 - p).
 NESLE_HD uint32_t sprite_pattern_row(const RenderView& s, uint32_t i, uint32_t r) {
     const uint8_t* so = s.oam + i * 4;
-    uint32_t lo = 0, hi = 0;
-    for (uint32_t sx = 0; sx < 8; ++sx) {
-        const uint32_t c = rv_sprite_px(s, so[1], so[2], sx, r);
-        lo |= (c & 1u) << sx;
-        hi |= (c >> 1) << sx;
+    const uint32_t tile = so[1], attr = so[2];
+    uint32_t base;
+    if (s.ctrl & 0x20) {  // 8x16
+        const uint32_t py = (attr & 0x80) ? 15u - r : r;
+        base = ((tile & 1u) ? 0x1000u : 0u) + (((tile & 0xFEu) + py / 8u) & 0xFFu) * 16u + (py & 7u);
+    } else {
+        const uint32_t py = (attr & 0x80) ? 7u - r : r;
+        base = ((s.ctrl & 0x08) ? 0x1000u : 0u) + tile * 16u + py;
+    }
+    uint32_t lo = rv_chr(s, base), hi = rv_chr(s, base + 8u);
+    if (!(attr & 0x40)) {
+        lo = reverse8(lo);
+        hi = reverse8(hi);
     }
     return lo | (hi << 8);
 }
