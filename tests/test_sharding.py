@@ -87,3 +87,13 @@ def test_shard_ranges_tile_the_global_range():
     ranges = [bench.shard(r, 65536)[1] for r in range(8)]
     cat = np.concatenate(ranges)
     np.testing.assert_array_equal(cat, np.arange(8 * 65536))
+
+
+@pytest.mark.parametrize("summary", ["step_kernel_config4.txt", "gray84_kernel_config3.txt",
+                                     "render_kernel_rgb_config3.txt"])
+def test_bench_reads_traffic_from_profile_summaries(summary):
+    """The bench line's roofline `traffic` comes from the committed ncu summaries."""
+    import bench
+
+    t = bench.profile_traffic(summary)
+    assert t is not None and t > 1e8, summary
