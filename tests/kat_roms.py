@@ -103,3 +103,37 @@ REWARD_CASES = [
     ((0, 80, 399), (0, 90, 398, 8), -1.0, 0),
     ((0, 48, 400), (0, 50, 399, 0x0B), -24.0, 1),
 ]
+
+
+# Render coverage beyond what snapshots alone reach (a warm reset zeroes the
+# scroll): PPUCTRL/PPUMASK from RAM $10/$11 (NMI and both layers forced on),
+# then $2005 rewritten in the main loop from RAM $12/$13, which also change
+# every pass, so the scroll latched at the frame's start and the one captured
+# at vblank differ (the two-region split).  The NMI handler DMAs OAM from page
+# $02 and moves sprite 0, so the split row changes from frame to frame.
+_RS_INIT = asm(0x8000, ("LDA", w.ZP, 0x10), ("ORA", w.IMM, 0x80), ("STA", w.ABS, 0x2000),
+               ("LDA", w.ZP, 0x11), ("ORA", w.IMM, 0x18), ("STA", w.ABS, 0x2001))
+_RS_LOOP = 0x8000 + len(_RS_INIT)
+RENDER_SCROLL_ROM = rom_with(
+    {0x8000: _RS_INIT + asm(_RS_LOOP, ("LDA", w.ZP, 0x12), ("STA", w.ABS, 0x2005), ("LDA", w.ZP, 0x13),
+                            ("STA", w.ABS, 0x2005), ("INC", w.ZP, 0x12), ("DEC", w.ZP, 0x13),
+                            ("JMP", w.ABS, _RS_LOOP)),
+     0x9000: asm(0x9000, ("PHA",), ("LDA", w.IMM, 0x02), ("STA", w.ABS, 0x4014), ("INC", w.ABS, 0x0203),
+                 ("INC", w.ABS, 0x0200), ("PLA",), ("RTI",))},
+    chr_rom=bytes(__import__("numpy").random.default_rng(77).integers(0, 256, 8192, dtype="uint8")))
+
+
+def render_scroll_snapshots(seed: int, k: int) -> list[bytes]:
+    """k snapshots at the ROM's reset code with random RAM (so random control,
+    mask and scroll bytes), nametables, palette and OAM."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    out = []
+    for i in range(k):
+        s = w.random_snapshot(seed + i, 0x8000, nmi_and_rendering=True)
+        s.nametable_ram = rng.integers(0, 256, 2048, dtype=np.uint8).tobytes()
+        s.palette_ram = rng.integers(0, 64, 32, dtype=np.uint8).tobytes()
+        s.oam = rng.integers(0, 256, 256, dtype=np.uint8).tobytes()
+        out.append(w.write_fcs(s))
+    return out

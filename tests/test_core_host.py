@@ -179,3 +179,22 @@ def test_illegal_opcode_freezes_env():
         h.step(np.zeros(2, np.uint8), auto_reset=False)
         assert_same(o, h)
     assert (h.get("status") == (0x80000000 | 0x020000 | 0x8002)).all()
+
+
+def test_render_scroll_split_matches_checker():
+    """Random control, mask and mid-frame scroll (two-region split with a moving
+    sprite 0), random CHR, nametables, palette and OAM: frames in all three
+    formats after every step."""
+    n = 16
+    snaps = kat.render_scroll_snapshots(5, 8)
+    kw = dict(env_to_level=np.arange(n) % 8)
+    o = Oracle(n, 4, kat.RENDER_SCROLL_ROM, snaps, **kw)
+    h = HostCore(n, 4, kat.RENDER_SCROLL_ROM, snaps, **kw)
+    for _ in range(3):
+        o.step(np.zeros(n, np.uint8), auto_reset=False)
+        h.step(np.zeros(n, np.uint8), auto_reset=False)
+        assert_same(o, h, label="render-scroll")
+        ro, rh = o.render(), h.render()
+        for k in ("index", "rgb", "gray84"):
+            np.testing.assert_array_equal(ro[k], rh[k], err_msg=k)
+    assert (o.get("snap_sx_start") != o.get("snap_sx_end")).any()

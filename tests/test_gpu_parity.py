@@ -264,3 +264,22 @@ def test_full_size_pixel_mode_matches_checker():
     _lib.check(g.lib.nesle_render(g._h, _lib.RENDER_GRAY84, None))
     full["gray84"] = g.get("obs_gray84")
     _windows_match(wl, full, [0, 32_768 - 16, n - 32], 32, 2, fields, render=True)
+
+
+@pytest.mark.parametrize("seed", [5, 6])
+def test_render_scroll_split_matches_checker(seed):
+    """The render kernels under random control, mask and mid-frame scroll (split
+    row moving with sprite 0), random CHR / nametables / palette / OAM: all three
+    observation formats after every step, 64 envs over 8 snapshots."""
+    n = 64
+    snaps = kat.render_scroll_snapshots(seed, 8)
+    kw = dict(env_to_level=np.arange(n) % 8)
+    o = Oracle(n, 4, kat.RENDER_SCROLL_ROM, snaps, **kw)
+    g = GpuCore(n, 4, kat.RENDER_SCROLL_ROM, snaps, **kw)
+    for _ in range(4):
+        o.step(np.zeros(n, np.uint8), auto_reset=False)
+        g.step(np.zeros(n, np.uint8), auto_reset=False)
+        assert_same(o, g, label="render-scroll")
+        ro, rg = o.render(), g.render()
+        for k in ("index", "rgb", "gray84"):
+            np.testing.assert_array_equal(ro[k], rg[k], err_msg=k)
