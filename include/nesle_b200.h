@@ -130,6 +130,14 @@ int nesle_save_states(nesle_batch* b, const uint32_t* envs, uint32_t count, int 
 int nesle_load_states(nesle_batch* b, const uint32_t* envs, uint32_t count, int envs_on_device, const void* src,
                       int src_on_device, void* stream);
 
+/* No counterpart in the reference (its observation copies land in pageable
+ * numpy arrays).  Page-locked host memory for the host-side copies of frames
+ * and observations: cudaHostAlloc with the portable flag, so every context of
+ * the process copies into it at the link's full rate.  The Python binding
+ * pools these buffers and hands each out as a fresh array. */
+int nesle_host_alloc(uint64_t bytes, void** out);
+int nesle_host_free(void* ptr);
+
 /* Replaces CudaBatch.poke_ram(address, value) (cuda_module.cu:939-945). */
 int nesle_poke_ram(nesle_batch* b, uint16_t address, uint8_t value, void* stream);
 

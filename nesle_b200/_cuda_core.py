@@ -24,13 +24,14 @@ from __future__ import annotations
 
 import ctypes
 import sys
+import weakref
 from typing import Any, Sequence
 
 import numpy as np
 
 from . import _lib
 
-__all__ = ["CudaBatch", "CudaDeviceArrayView", "parse_fcs_state"]
+__all__ = ["CudaBatch", "CudaDeviceArrayView", "parse_fcs_state", "release_host_buffers"]
 
 _TYPESTR_DTYPE = {"|u1": np.uint8, "<u1": np.uint8, "<f4": np.float32}
 _LEGACY_STREAM = 1  # cudaStreamLegacy
@@ -38,6 +39,47 @@ _LEGACY_STREAM = 1  # cudaStreamLegacy
 
 def _torch():
     return sys.modules.get("torch")
+
+
+class _HostBuffers:
+    """Page-locked host buffers (nesle_host_alloc) for frame and observation
+    copies, recycled by size.  Each call hands out a fresh array; its buffer
+    goes back to the free list only when the array and every view of it are
+    gone, so results never alias.  A device-to-host copy into page-locked memory
+    runs at the link's rate (57 GB/s measured on B200), 10-25x a pageable one."""
+
+    def __init__(self) -> None:
+        self._free: dict[int, list[int]] = {}
+
+    def array(self, lib, shape: tuple[int, ...], dtype) -> np.ndarray:
+        nbytes = int(np.prod(shape)) * np.dtype(dtype).itemsize
+        free = self._free.get(nbytes)
+        ptr = free.pop() if free else None  # list.pop is atomic under the GIL
+        if ptr is None:
+            p = ctypes.c_void_p()
+            _lib.check(lib.nesle_host_alloc(nbytes, ctypes.byref(p)))
+            ptr = int(p.value)
+        holder = (ctypes.c_uint8 * nbytes).from_address(ptr)
+        fin = weakref.finalize(holder, self._give_back, nbytes, ptr)
+        fin.atexit = False  # the process releases page-locked memory at exit
+        return np.frombuffer(holder, dtype=dtype).reshape(shape)
+
+    def _give_back(self, nbytes: int, ptr: int) -> None:
+        self._free.setdefault(nbytes, []).append(ptr)
+
+    def release(self, lib) -> None:
+        """Free every buffer no array holds any more."""
+        for ptrs in self._free.values():
+            while ptrs:
+                lib.nesle_host_free(ctypes.c_void_p(ptrs.pop()))
+
+
+_HOST_BUFFERS = _HostBuffers()
+
+
+def release_host_buffers() -> None:
+    """Return the pooled page-locked frame/observation buffers to the system."""
+    _HOST_BUFFERS.release(_lib.load())
 
 
 def _current_stream(device: int) -> int:
@@ -188,15 +230,12 @@ class CudaBatch:
         return self._ptr_cache[which]
 
     def _field(self, name: str, pinned: bool = False) -> np.ndarray:
-        """Host copy of a per-env field.  ``pinned`` (large frame copies) lands it
-        in page-locked memory from torch's caching host allocator, which the
-        DMA engine fills at full speed; the array is still a fresh one."""
+        """Host copy of a per-env field, as a fresh array.  ``pinned`` (large
+        frame and observation copies) lands it in a pooled page-locked buffer
+        (_HostBuffers), which the DMA engine fills at full speed."""
         dtype, shape = _lib.FIELDS[name]
-        torch = _torch() if pinned else None
-        if torch is not None and torch.cuda.is_available():
-            nbytes = int(np.prod((self.num_envs, *shape))) * np.dtype(dtype).itemsize
-            out = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True).numpy().view(dtype)
-            out = out.reshape((self.num_envs, *shape))
+        if pinned:
+            out = _HOST_BUFFERS.array(self._lib, (self.num_envs, *shape), dtype)
         else:
             out = np.empty((self.num_envs, *shape), dtype=dtype)
         self._check(self._lib.nesle_copy_field(self._h, name.encode(), out.ctypes.data, out.nbytes))

@@ -60,6 +60,8 @@ SIGNATURES = {
                                   ctypes.c_int, ctypes.c_void_p]),
     "nesle_step_profile": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "nesle_host_alloc": (ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]),
+    "nesle_host_free": (ctypes.c_int, [ctypes.c_void_p]),
     "nesle_state_bytes": (ctypes.c_uint64, []),
     "nesle_save_states": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int,
                                          ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),

@@ -428,6 +428,18 @@ int nesle_render(nesle_batch* b, int mode, void* stream) {
     return finish(b, s, launch_render(b->dv, b->n, out, mode, s), "render kernel");
 }
 
+int nesle_host_alloc(uint64_t bytes, void** out) {
+    if (!out || !bytes) return fail(NESLE_ERR_INVALID, "host_alloc: null output or zero size");
+    *out = nullptr;
+    CUDA_TRY(cudaHostAlloc(out, bytes, cudaHostAllocPortable), "host alloc");
+    return NESLE_OK;
+}
+
+int nesle_host_free(void* ptr) {
+    if (ptr) CUDA_TRY(cudaFreeHost(ptr), "host free");
+    return NESLE_OK;
+}
+
 uint64_t nesle_state_bytes(void) { return kStateBytes; }
 
 static int state_io(nesle_batch* b, const uint32_t* envs, uint32_t count, int envs_on_device, void* blobs,

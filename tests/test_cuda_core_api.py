@@ -294,3 +294,40 @@ def test_render_after_step_matches_inline_render(torch):
     fa = a.render()
     np.testing.assert_array_equal(fa, out["obs"])
     assert int((fa != first).sum()) > 100  # the frame moved on
+
+
+@pytest.mark.gpu
+def test_observation_arrays_are_fresh_and_their_buffers_recycled(torch):
+    """Host observations come from pooled page-locked buffers: every step hands
+    out a new array (a kept one is never overwritten), and a buffer is reused
+    only after the array made from it is dropped."""
+    import gc
+
+    from nesle_b200 import _cuda_core
+
+    n = 16
+    b, wl, env = _batch(n)
+    o = _oracle(n, wl)
+    kept = []
+    for s in range(3):
+        a = wl.actions(env, s)
+        out = b.step(a, obs_mode="gray84")
+        o.step(a, device_api=False, auto_reset=False)
+        want = o.render()["gray84"]
+        np.testing.assert_array_equal(out["obs"], want)
+        kept.append((out["obs"], want))
+    assert len({k[0].ctypes.data for k in kept}) == 3
+    for got, want in kept:  # later steps did not write into earlier arrays
+        np.testing.assert_array_equal(got, want)
+    used = {k[0].ctypes.data for k in kept}
+    kept.clear()
+    out = got = want = None
+    gc.collect()
+    assert used <= set(_cuda_core._HOST_BUFFERS._free.get(n * 84 * 84, []))
+    out = b.step(wl.actions(env, 3), obs_mode="gray84")
+    assert out["obs"].ctypes.data in used  # a dropped buffer, not a new allocation
+    o.step(wl.actions(env, 3), device_api=False, auto_reset=False)
+    np.testing.assert_array_equal(out["obs"], o.render()["gray84"])
+    out = None
+    _cuda_core.release_host_buffers()
+    assert not _cuda_core._HOST_BUFFERS._free.get(n * 84 * 84)
