@@ -902,11 +902,7 @@ NESLE_HD uint32_t exec_uniform(const Ctx& c, Lane& L, Fetched& f, bool& fresh) {
     uint32_t m = (is_ram || is_prg) ? mem : (is_ctrl ? (0x40u | cbit) : (addr == 0x4017u ? 0x41u : 0u));
     m = (w0 & E0_IMM) ? b1 : m;
     const bool io_space = (addr - 0x2000u < 0x2000u) || (addr - 0x6000u < 0x2000u);
-    bool side = false;
-    if (rd && io_space) {
-        m = io_rd(c, L, addr);
-        side = true;
-    }
+    if (rd && io_space) m = io_rd(c, L, addr);
     const bool shift_now = rd && is_ctrl && !L.cstrobe && L.csr > 1u;  // batch_bus.cuh:115-121
     L.csr = shift_now ? (L.csr >> 1) : L.csr;
 
@@ -937,17 +933,16 @@ NESLE_HD uint32_t exec_uniform(const Ctx& c, Lane& L, Fetched& f, bool& fresh) {
     const bool latch = cw && ((r & 1u) || L.cstrobe);
     L.csr = latch ? L.action : L.csr;
     L.cstrobe = cw ? (r & 1u) : L.cstrobe;
-    if (wm && (io_space || addr == 0x4014u)) {
-        io_wr(c, L, addr, r);
-        side = true;
-    }
+    if (wm && (io_space || addr == 0x4014u)) io_wr(c, L, addr, r);
 
     // ---- register write-back ----
     L.R = ((R & ~wmask) | ((r * 0x01010101u) & wmask)) + spd;
     L.p = p;
     L.pc = npc;
     f = nf;
-    fresh = in_prg_window(npc) && !side;
+    // The prefetch stays valid after I/O side effects (PRG ROM cannot change);
+    // only a pending NMI, which a $2000 write can raise, needs the loop top.
+    fresh = in_prg_window(npc) && !L.nmi;
     return cyc;
 }
 
@@ -1053,7 +1048,8 @@ NESLE_HD void run_frames(const Ctx& c, Lane& L, const Prof& prof = Prof()) {
             }
             exec_special(c, L, op, f.b1, f.b2);
             it_cyc += byte_of(f.e.w[0], 3);
-            fresh = false;
+            fresh = in_prg_window(L.pc) && !L.nmi;
+            if (fresh) fetch_prg(c, L.pc, f);
         } else {
             it_cyc += exec_uniform<kSharedRam>(c, L, f, fresh);
         }
