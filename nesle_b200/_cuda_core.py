@@ -458,9 +458,12 @@ class CudaBatch:
             self._check(self._lib.nesle_render(self._h, _lib.RENDER_GRAY84, ctypes.c_void_p(self._stream())))
         return self._view(_lib.PTR_OBS_GRAY84, (self.num_envs, 84, 84), "|u1")
 
+    _FRAME_FIELDS = frozenset(("frames_rgb", "frames_index", "obs_gray84"))
+
     def get_field(self, name: str) -> np.ndarray:
-        """Host copy of any per-env field of the C ABI (nesle_copy_field)."""
-        return self._field(name)
+        """Host copy of any per-env field of the C ABI (nesle_copy_field), as a
+        fresh array; frames and observations land in pooled page-locked buffers."""
+        return self._field(name, pinned=name in self._FRAME_FIELDS)
 
     # -- helpers ----------------------------------------------------------
     def _copy_frames(self) -> np.ndarray:

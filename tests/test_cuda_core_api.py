@@ -331,3 +331,46 @@ def test_observation_arrays_are_fresh_and_their_buffers_recycled(torch):
     out = None
     _cuda_core.release_host_buffers()
     assert not _cuda_core._HOST_BUFFERS._free.get(n * 84 * 84)
+
+
+def test_host_buffer_pool_recycles_only_dropped_arrays():
+    """The page-locked pool (with a fake allocator, no GPU): arrays are fresh,
+    a buffer comes back only when its last array or view is gone, and
+    release() frees what the pool holds."""
+    import ctypes
+    import gc
+
+    from nesle_b200._cuda_core import _HostBuffers
+
+    keep, freed = [], []
+
+    class FakeLib:
+        def nesle_host_alloc(self, nbytes, out):
+            buf = ctypes.create_string_buffer(int(nbytes))
+            keep.append(buf)
+            out._obj.value = ctypes.addressof(buf)
+            return 0
+
+        def nesle_host_free(self, ptr):
+            freed.append(ptr.value)
+            return 0
+
+    pool, lib = _HostBuffers(), FakeLib()
+    a = pool.array(lib, (4, 8), np.uint8)
+    b = pool.array(lib, (4, 8), np.uint8)
+    assert a.ctypes.data != b.ctypes.data and len(keep) == 2
+    a[:] = 1
+    b[:] = 2
+    pa = a.ctypes.data
+    view = b[1:]
+    del a, b
+    gc.collect()
+    assert pool._free[32] == [pa]  # b's buffer is still held by `view`
+    c = pool.array(lib, (4, 8), np.uint8)
+    assert c.ctypes.data == pa and len(keep) == 2  # reused, not allocated
+    assert (view == 2).all()
+    del view, c
+    gc.collect()
+    assert sorted(pool._free[32]) == sorted([pa, ctypes.addressof(keep[1])])
+    pool.release(lib)
+    assert not pool._free[32] and sorted(freed) == sorted([pa, ctypes.addressof(keep[1])])
