@@ -130,6 +130,15 @@ int nesle_save_states(nesle_batch* b, const uint32_t* envs, uint32_t count, int 
 int nesle_load_states(nesle_batch* b, const uint32_t* envs, uint32_t count, int envs_on_device, const void* src,
                       int src_on_device, void* stream);
 
+/* Replaces the render + copy inside CudaBatch.step(copy_obs=True) and render()
+ * (cuda_module.cu:566-588, 820-840): the frames (`mode` as nesle_render) of
+ * every env rendered and copied into `host_out` (num_envs x bytes per env).
+ * The work is split into 8 env ranges; each range is copied on a stream of the
+ * batch's own as soon as it is rendered, so copies overlap rendering.  Returns
+ * when the copies are complete.  Page-locked `host_out` (nesle_host_alloc)
+ * copies at the link's full rate. */
+int nesle_render_copy(nesle_batch* b, int mode, void* host_out, uint64_t bytes, void* stream);
+
 /* No counterpart in the reference (its observation copies land in pageable
  * numpy arrays).  Page-locked host memory for the host-side copies of frames
  * and observations: cudaHostAlloc with the portable flag, so every context of

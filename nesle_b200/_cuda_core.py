@@ -278,15 +278,22 @@ class CudaBatch:
         a = self._host_actions(actions)
         s = ctypes.c_void_p(self._stream())
         self._check(self._lib.nesle_step(self._h, a.ctypes.data, _lib.ACTIONS_U8, 0, 0, 0, s))
-        if render_frame or copy_obs:
-            self._check(self._lib.nesle_render(self._h, mode, s))
-        self.synchronize()
         out = {}
         if copy_obs:
-            out["obs"] = self._field(field, pinned=True)
+            out["obs"] = self._render_copy(mode, field, s)
+        elif render_frame:
+            self._check(self._lib.nesle_render(self._h, mode, s))
+        self.synchronize()
         out["rewards"] = self._field("rewards")
         out["dones"] = self._field("done")
         return out
+
+    def _render_copy(self, mode: int, field: str, stream: ctypes.c_void_p) -> np.ndarray:
+        """Render and copy to a fresh page-locked array in one pipelined call."""
+        dtype, shape = _lib.FIELDS[field]
+        arr = _HOST_BUFFERS.array(self._lib, (self.num_envs, *shape), dtype)
+        self._check(self._lib.nesle_render_copy(self._h, mode, arr.ctypes.data, arr.nbytes, stream))
+        return arr
 
     def step_launch(self, actions: Any) -> None:
         """Extension: the kernel of step() on the current stream (host actions
@@ -327,9 +334,10 @@ class CudaBatch:
                 "budget_hits": self._field("stat_budget_hits"), "opcode_counts": ops, "pc_counts": pcs}
 
     def render(self) -> np.ndarray:
-        self.render_device()
-        self.synchronize()
-        return self._copy_frames()
+        """RGB frames (N, 240, 256, 3), re-rendered (cuda_module.cu:820-840)."""
+        out = self._render_copy(_lib.RENDER_RGB, "frames_rgb", ctypes.c_void_p(self._stream()))
+        self._raise_on_fault()
+        return out
 
     def render_device(self) -> None:
         self._check(self._lib.nesle_render(self._h, _lib.RENDER_RGB, ctypes.c_void_p(self._stream())))
@@ -466,9 +474,6 @@ class CudaBatch:
         return self._field(name, pinned=name in self._FRAME_FIELDS)
 
     # -- helpers ----------------------------------------------------------
-    def _copy_frames(self) -> np.ndarray:
-        return self._field("frames_rgb", pinned=True)
-
     def _device_actions(self, actions: Any) -> tuple[int, int]:
         """(pointer, dtype code) of CUDA actions (cuda_module.cu:259-308)."""
         if hasattr(actions, "data_ptr") and hasattr(actions, "is_cuda"):

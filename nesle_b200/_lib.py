@@ -68,6 +68,8 @@ SIGNATURES = {
     "nesle_load_states": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int,
                                          ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "nesle_render": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "nesle_render_copy": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64,
+                                         ctypes.c_void_p]),
     "nesle_render_gray84_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
                                                    ctypes.c_void_p]),
     "nesle_poke_ram": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint16, ctypes.c_uint8, ctypes.c_void_p]),

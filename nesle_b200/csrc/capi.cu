@@ -49,6 +49,8 @@ int bcd3(const uint8_t* ram, int a) { return (ram[a] & 0xF) * 100 + (ram[a + 1] 
 
 }  // namespace
 
+constexpr uint32_t kRenderChunks = 8;  // env ranges of nesle_render_copy
+
 struct nesle_batch {
     int device = 0;
     uint32_t n = 0, frameskip = 0, num_levels = 0;
@@ -65,6 +67,8 @@ struct nesle_batch {
     uint8_t* d_state_blobs = nullptr;
     uint32_t state_cap = 0;
     cudaEvent_t done_event = nullptr;
+    cudaStream_t copy_stream = nullptr;         // nesle_render_copy: device-to-host copies
+    cudaEvent_t chunk_events[kRenderChunks] = {};  // nesle_render_copy: one per rendered range
     uint32_t step_variant = kStepGlobalRam;
     uint32_t step_threads = 0;
 
@@ -92,6 +96,12 @@ struct nesle_batch {
         allocations.clear();
         if (done_event) cudaEventDestroy(done_event);
         done_event = nullptr;
+        for (cudaEvent_t& e : chunk_events) {
+            if (e) cudaEventDestroy(e);
+            e = nullptr;
+        }
+        if (copy_stream) cudaStreamDestroy(copy_stream);
+        copy_stream = nullptr;
     }
 };
 
@@ -425,7 +435,42 @@ int nesle_render(nesle_batch* b, int mode, void* stream) {
     TRY(ensure_frames(b, which));
     uint8_t* out = mode == NESLE_RENDER_RGB ? b->d_frames_rgb : mode == NESLE_RENDER_INDEX ? b->d_frames_index : b->d_gray84;
     auto s = static_cast<cudaStream_t>(stream);
-    return finish(b, s, launch_render(b->dv, b->n, out, mode, s), "render kernel");
+    return finish(b, s, launch_render(b->dv, 0, b->n, out, mode, s), "render kernel");
+}
+
+// Rendered in kRenderChunks env ranges on `stream`; each range's rows are
+// copied to the host on the batch's copy stream as soon as they are done, so
+// the copy of one range overlaps the rendering of the next.
+int nesle_render_copy(nesle_batch* b, int mode, void* host_out, uint64_t bytes, void* stream) {
+    if (!b || !host_out) return fail(NESLE_ERR_INVALID, "render_copy: null argument");
+    if (mode < NESLE_RENDER_RGB || mode > NESLE_RENDER_GRAY84) return fail(NESLE_ERR_INVALID, "unknown render mode");
+    const uint64_t per_env = mode == NESLE_RENDER_RGB ? (uint64_t)kFrameW * kFrameH * 3
+                             : mode == NESLE_RENDER_INDEX ? (uint64_t)kFrameW * kFrameH : (uint64_t)kGray * kGray;
+    if (bytes != (uint64_t)b->n * per_env) return fail(NESLE_ERR_INVALID, "render_copy: wrong output size");
+    DeviceGuard guard(b->device);
+    const int which = mode == NESLE_RENDER_RGB ? NESLE_PTR_FRAMES_RGB
+                      : mode == NESLE_RENDER_INDEX ? NESLE_PTR_FRAMES_INDEX : NESLE_PTR_OBS_GRAY84;
+    TRY(ensure_frames(b, which));
+    uint8_t* dev = mode == NESLE_RENDER_RGB ? b->d_frames_rgb : mode == NESLE_RENDER_INDEX ? b->d_frames_index : b->d_gray84;
+    if (!b->copy_stream) CUDA_TRY(cudaStreamCreateWithFlags(&b->copy_stream, cudaStreamNonBlocking), "copy stream");
+    for (cudaEvent_t& e : b->chunk_events)
+        if (!e) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "chunk event");
+    auto s = static_cast<cudaStream_t>(stream);
+    const uint32_t per_chunk = (b->n + kRenderChunks - 1) / kRenderChunks;
+    auto* host = static_cast<uint8_t*>(host_out);
+    for (uint32_t k = 0; k < kRenderChunks; ++k) {
+        const uint32_t env0 = k * per_chunk;
+        if (env0 >= b->n) break;
+        const uint32_t count = per_chunk < b->n - env0 ? per_chunk : b->n - env0;
+        CUDA_TRY(launch_render(b->dv, env0, count, dev, mode, s), "render kernel");
+        CUDA_TRY(cudaEventRecord(b->chunk_events[k], s), "record chunk event");
+        CUDA_TRY(cudaStreamWaitEvent(b->copy_stream, b->chunk_events[k], 0), "copy stream wait");
+        CUDA_TRY(cudaMemcpyAsync(host + env0 * per_env, dev + env0 * per_env, count * per_env, cudaMemcpyDeviceToHost,
+                                 b->copy_stream), "copy rendered chunk");
+    }
+    CUDA_TRY(cudaEventRecord(b->done_event, s), "record event");
+    CUDA_TRY(cudaStreamSynchronize(b->copy_stream), "synchronize copies");
+    return NESLE_OK;
 }
 
 int nesle_host_alloc(uint64_t bytes, void** out) {
@@ -619,7 +664,7 @@ int nesle_render_gray84_noalloc(nesle_batch* b, uint8_t* host_out, uint64_t byte
     uint8_t* scratch = nullptr;
     TRY(noalloc_scratch(b->device, &scratch));
     auto s = static_cast<cudaStream_t>(stream);
-    CUDA_TRY(launch_render(b->dv, b->n, scratch, NESLE_RENDER_GRAY84, s), "render_gray84_noalloc kernel");
+    CUDA_TRY(launch_render(b->dv, 0, b->n, scratch, NESLE_RENDER_GRAY84, s), "render_gray84_noalloc kernel");
     CUDA_TRY(cudaMemcpyAsync(host_out, scratch, bytes, cudaMemcpyDeviceToHost, s), "render_gray84_noalloc copy");
     CUDA_TRY(cudaStreamSynchronize(s), "render_gray84_noalloc synchronize");
     return NESLE_OK;

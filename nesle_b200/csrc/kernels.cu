@@ -432,7 +432,7 @@ __device__ __forceinline__ void render_strip(const RenderEnv& e, const SnapSmem&
 // 8-byte (RGB) stores, each warp covering a contiguous stretch of the frame.
 constexpr uint32_t kRenderStripRows = 20;
 __global__ void __launch_bounds__(kRenderThreads, kRenderMinBlocks)
-render_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint32_t rgb) {
+render_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint32_t rgb, uint32_t env0) {
     __shared__ __align__(16) SnapSmem sm;
     __shared__ uint32_t s_tiles[kRenderStripRows * kRowTiles];
     __shared__ __align__(16) uint8_t s_buf[kRenderStripRows * kFrameW];
@@ -441,7 +441,7 @@ render_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint3
     __shared__ uint32_t s_group[4];
     __shared__ uint32_t s_count;
     const BatchView& v = *vp;
-    const uint32_t env = blockIdx.x, tid = threadIdx.x;
+    const uint32_t env = env0 + blockIdx.x, tid = threadIdx.x;
     if (tid < 64)
         s_rgb[tid] = kPaletteRgb[tid * 3] | ((uint32_t)kPaletteRgb[tid * 3 + 1] << 8) |
                      ((uint32_t)kPaletteRgb[tid * 3 + 2] << 16);
@@ -511,11 +511,11 @@ __device__ __forceinline__ uint32_t span_weights(uint32_t first, uint32_t unit, 
 }
 
 __global__ void __launch_bounds__(kRenderThreads, kGrayMinBlocks)
-gray84_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out) {
+gray84_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint32_t env0) {
     __shared__ __align__(16) SnapSmem sm;
     __shared__ Gray84Smem g;
     const BatchView& v = *vp;
-    const uint32_t env = blockIdx.x, tid = threadIdx.x;
+    const uint32_t env = env0 + blockIdx.x, tid = threadIdx.x;
     if (tid < 64) g.lut[tid] = (uint8_t)luma_of_rgb(kPaletteRgb[tid * 3], kPaletteRgb[tid * 3 + 1], kPaletteRgb[tid * 3 + 2]);
     if (tid < kGray) {
         g.hx[tid] = span_weights(64u * tid / 21u, 21u, 64u * tid, 64u * tid + 64u);
@@ -616,11 +616,13 @@ cudaError_t launch_poke(const BatchView* dv, uint32_t num_envs, uint32_t address
     return cudaGetLastError();
 }
 
-cudaError_t launch_render(const BatchView* dv, uint32_t num_envs, uint8_t* out, int mode, cudaStream_t s) {
+// Envs [env0, env0 + count) into their rows of `out` (row = env index).
+cudaError_t launch_render(const BatchView* dv, uint32_t env0, uint32_t count, uint8_t* out, int mode, cudaStream_t s) {
+    if (!count) return cudaSuccess;
     if (mode == 2) {
-        gray84_kernel<<<num_envs, kRenderThreads, 0, s>>>(dv, out);
+        gray84_kernel<<<count, kRenderThreads, 0, s>>>(dv, out, env0);
     } else {
-        render_kernel<<<num_envs, kRenderThreads, 0, s>>>(dv, out, mode == 0 ? 1u : 0u);
+        render_kernel<<<count, kRenderThreads, 0, s>>>(dv, out, mode == 0 ? 1u : 0u, env0);
     }
     return cudaGetLastError();
 }

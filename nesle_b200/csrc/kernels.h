@@ -27,6 +27,6 @@ cudaError_t launch_reset(const BatchView* dv, uint32_t num_envs, const uint8_t* 
 cudaError_t launch_state(const BatchView* dv, const uint32_t* envs, uint32_t count, uint8_t* blobs, bool save,
                          cudaStream_t s);
 cudaError_t launch_poke(const BatchView* dv, uint32_t num_envs, uint32_t address, uint32_t value, cudaStream_t s);
-cudaError_t launch_render(const BatchView* dv, uint32_t num_envs, uint8_t* out, int mode, cudaStream_t s);
+cudaError_t launch_render(const BatchView* dv, uint32_t env0, uint32_t count, uint8_t* out, int mode, cudaStream_t s);
 
 }  // namespace nesle

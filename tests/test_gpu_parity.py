@@ -283,3 +283,25 @@ def test_render_scroll_split_matches_checker(seed):
         ro, rg = o.render(), g.render()
         for k in ("index", "rgb", "gray84"):
             np.testing.assert_array_equal(ro[k], rg[k], err_msg=k)
+
+
+@pytest.mark.parametrize("n", [3, 37])
+def test_render_copy_matches_render_then_copy(n):
+    """nesle_render_copy (8 env ranges, each copied while the next renders) gives
+    the bytes of nesle_render + nesle_copy_field, also for batches whose ranges
+    are ragged (37 envs) or fewer than 8 (3 envs)."""
+    from test_core_host import render_snapshots
+
+    wl = w.config4()
+    snaps = render_snapshots(11, 4, wl.rom.loop_head)
+    g = GpuCore(n, 4, wl.rom.image, snaps, env_to_level=np.arange(n) % 4, done_mode=wl.done_mode,
+                done_args=wl.done_args, seed=wl.seed)
+    g.step(wl.actions(np.arange(n), 0))
+    want = g.render()
+    for mode, key, field in ((_lib.RENDER_RGB, "rgb", "frames_rgb"), (_lib.RENDER_INDEX, "index", "frames_index"),
+                             (_lib.RENDER_GRAY84, "gray84", "obs_gray84")):
+        dtype, shape = _lib.FIELDS[field]
+        out = np.full((n, *shape), 0xAB, dtype)
+        _lib.check(g.lib.nesle_render_copy(g._h, mode, out.ctypes.data, out.nbytes, None))
+        np.testing.assert_array_equal(out, want[key], err_msg=key)
+        assert g.lib.nesle_render_copy(g._h, mode, out.ctypes.data, out.nbytes - 1, None) == _lib.NESLE_ERR_INVALID
