@@ -379,18 +379,84 @@ __device__ __forceinline__ uint32_t group_colors(const SnapSmem& sm, uint32_t gr
     return w;
 }
 
-// Colour index of pixel (x, y) with the sprites `spr` that may cover it.
-__device__ __forceinline__ uint32_t sprite_pixel(const RenderEnv& e, const SnapSmem& sm, const uint32_t* tiles,
-                                                 uint32_t x, uint32_t y, uint64_t spr) {
+// The 8 pixels of a segment that sprites may cover, as compose_pixel_tables
+// gives them pixel by pixel, with each sprite applied to all 8 at once: in
+// index order a sprite claims the pixels not yet claimed where it is opaque and
+// eligible (in front, or behind a background of colour 0).  Colour indices
+// packed one per byte (pixel p in byte p), or their luma with kLuma.
+template <bool kLuma>
+__device__ __forceinline__ uint64_t sprite_segment(const RenderEnv& e, const SnapSmem& sm, const uint32_t* tiles,
+                                                   const uint8_t* lut, uint32_t y, uint32_t c8, uint64_t spr) {
     const RenderView& bv = bg_view(e, y);
-    const uint32_t bgc = bg_from_entry_tables(bv, sm.res, tiles[tile_slot(bv, x)], x, bv.sx + x);
-    return compose_pixel_tables(e, sm.res, x, y, bgc, spr, sm.spat);
+    const RenderView& s = e.lower;
+    const uint32_t x0 = 8u * c8;
+    uint32_t lo8 = 0, hi8 = 0, grp0 = 0, grp1 = 0, keep = 8;
+    if ((bv.mask & 0x08) && ((bv.mask & 0x02) || c8 != 0)) {
+        const uint32_t e0 = tiles[c8], e1 = tiles[c8 + 1], fine = bv.sx & 7u;
+        lo8 = ((((e0 & 0xFFu) << 8) | (e1 & 0xFFu)) << fine >> 8) & 0xFFu;  // pixel p at bit 7 - p
+        hi8 = (((e0 & 0xFF00u) | ((e1 >> 8) & 0xFFu)) << fine >> 8) & 0xFFu;
+        grp0 = (e0 >> 16) & 3u;
+        grp1 = (e1 >> 16) & 3u;
+        keep = 8u - fine;
+    }
+    uint64_t bg = 0;    // background colour index of pixel p in byte p (0: transparent)
+    uint32_t bgop = 0;  // bit p: the background a behind-background sprite is tested against is non-zero
+#pragma unroll
+    for (uint32_t p = 0; p < 8; ++p) {
+        const uint32_t col = ((lo8 >> (7 - p)) & 1u) | (((hi8 >> (7 - p)) & 1u) << 1);
+        const uint32_t bgc = col ? sm.res[(p < keep ? grp0 : grp1) * 4u + col] : 0u;
+        bg |= (uint64_t)bgc << (8 * p);
+        bgop |= (bgc != 0u ? 1u : 0u) << p;
+    }
+    bool bgop_ready = (int)y >= e.split;  // above the split the reference tests the lower view's background
+    uint64_t spc = 0;                      // colour of the claiming sprite, byte p
+    uint32_t claimed = 0;
+    while (spr && claimed != 0xFFu) {
+        const uint32_t i = lowest_set(spr);
+        spr &= spr - 1;
+        const uint8_t* so = s.oam + i * 4;
+        const int d = (int)so[3] - (int)x0;  // segment pixel of the sprite's column 0 (-7..7)
+        const uint32_t pat = sm.spat[i * 16 + (y - so[0] - 1)];
+        uint32_t plo = pat & 0xFFu, phi = pat >> 8;  // sprite pixel sx at bit sx
+        if (d >= 0) {
+            plo = (plo << d) & 0xFFu;
+            phi = (phi << d) & 0xFFu;
+        } else {
+            plo >>= -d;
+            phi >>= -d;
+        }
+        uint32_t take = (plo | phi) & ~claimed;
+        const uint32_t attr = so[2];
+        if (take && (attr & 0x20)) {
+            if (!bgop_ready) {
+                bgop = 0;
+                for (uint32_t p = 0; p < 8; ++p) bgop |= (rv_background(s, x0 + p, y) != 0 ? 1u : 0u) << p;
+                bgop_ready = true;
+            }
+            take &= ~bgop;
+        }
+        if (!take) continue;
+        claimed |= take;
+        const uint8_t* pal = sm.res + 0x10 + (attr & 3u) * 4u;
+#pragma unroll
+        for (uint32_t p = 0; p < 8; ++p)
+            if ((take >> p) & 1u) spc |= (uint64_t)pal[((plo >> p) & 1u) | (((phi >> p) & 1u) << 1)] << (8 * p);
+    }
+    uint64_t out = 0;
+#pragma unroll
+    for (uint32_t p = 0; p < 8; ++p) {
+        const uint32_t b = (uint32_t)(bg >> (8 * p)) & 0xFFu;
+        const uint32_t c = ((claimed >> p) & 1u) ? (uint32_t)(spc >> (8 * p)) & 0xFFu : (b ? b : (uint32_t)sm.res[0]);
+        out |= (uint64_t)(kLuma ? (uint32_t)lut[c] : c) << (8 * p);
+    }
+    return out;
 }
 
 // One strip of `rows` rows into `buf` (row r at buf + r * 256): tile entries,
 // then (A) every 8-column segment from the tile entries, listing the segments
-// a sprite may cover, then (B) those segments' pixels one per thread, composed
-// with the sprites.  kLuma stores luma (lut[colour]) instead of colours.
+// a sprite may cover, then (B) those segments again, one per thread, composed
+// with the sprites (sprite_segment).  kLuma stores luma (lut[colour]) instead
+// of colours.
 // Ends with a barrier; `list` holds rows * 32 entries.
 template <bool kLuma>
 __device__ __forceinline__ void render_strip(const RenderEnv& e, const SnapSmem& sm, uint32_t* tiles, uint32_t row0,
@@ -418,11 +484,11 @@ __device__ __forceinline__ void render_strip(const RenderEnv& e, const SnapSmem&
         }
     }
     __syncthreads();
-    const uint32_t tasks = count * 8u;
+    const uint32_t tasks = count;
     for (uint32_t t = tid; t < tasks; t += blockDim.x) {
-        const uint32_t sg = list[t >> 3], r = sg >> 5, c8 = sg & 31u, x = 8u * c8 + (t & 7u), y = row0 + r;
-        const uint32_t c = sprite_pixel(e, sm, tiles + r * kRowTiles, x, y, sm.rows[y] & sm.cols[c8]);
-        buf[r * kFrameW + x] = (uint8_t)(kLuma ? lut[c] : c);
+        const uint32_t sg = list[t], r = sg >> 5, c8 = sg & 31u, y = row0 + r;
+        const uint64_t px = sprite_segment<kLuma>(e, sm, tiles + r * kRowTiles, lut, y, c8, sm.rows[y] & sm.cols[c8]);
+        *reinterpret_cast<uint2*>(buf + r * kFrameW + 8u * c8) = make_uint2((uint32_t)px, (uint32_t)(px >> 32));
     }
     __syncthreads();
 }
