@@ -598,18 +598,26 @@ gray84_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint3
     uint8_t* dst = out + (size_t)env * kGray * kGray;
     for (uint32_t k = 0; k < kFrameH / kG84Rows; ++k) {
         render_strip<true>(e, sm, g.tiles, k * kG84Rows, kG84Rows, g.group_luma, g.lut, g.luma, g.list, g.count);
-        for (uint32_t i = tid; i < kG84Rows * kGray; i += kRenderThreads) {
-            const uint32_t r = i / kGray, ox = i - r * kGray, w = g.hx[ox];
-            const uint8_t* l = &g.luma[r * kFrameW + (w & 0xFFu)];
-            g.h[r][ox] = (uint16_t)(l[0] * ((w >> 8) & 31u) + l[1] * ((w >> 13) & 31u) + l[2] * ((w >> 18) & 31u) +
-                                    l[3] * ((w >> 23) & 31u));
+        // Threads 0..251: output column ox = tid % 84, every third row from tid / 84,
+        // so each thread decodes its column's weights once.
+        if (tid < 3 * kGray) {
+            const uint32_t ox = tid % kGray, first = tid / kGray, w = g.hx[ox];
+            const uint32_t w0 = (w >> 8) & 31u, w1 = (w >> 13) & 31u, w2 = (w >> 18) & 31u, w3 = (w >> 23) & 31u;
+            const uint8_t* l = &g.luma[w & 0xFFu];
+            for (uint32_t r = first; r < kG84Rows; r += 3) {
+                const uint8_t* q = l + r * kFrameW;
+                g.h[r][ox] = (uint16_t)(q[0] * w0 + q[1] * w1 + q[2] * w2 + q[3] * w3);
+            }
         }
         __syncthreads();
-        for (uint32_t i = tid; i < kG84Out * kGray; i += kRenderThreads) {
-            const uint32_t oyl = i / kGray, ox = i - oyl * kGray, w = g.vy[oyl], r = w & 0xFFu;
-            const uint32_t acc = g.h[r][ox] * ((w >> 8) & 31u) + g.h[r + 1][ox] * ((w >> 13) & 31u) +
-                                 g.h[r + 2][ox] * ((w >> 18) & 31u) + g.h[r + 3][ox] * ((w >> 23) & 31u);
-            dst[(k * kG84Out + oyl) * kGray + ox] = (uint8_t)((acc + 640u) / 1280u);
+        if (tid < 3 * kGray) {
+            const uint32_t ox = tid % kGray;
+            for (uint32_t oyl = tid / kGray; oyl < kG84Out; oyl += 3) {
+                const uint32_t w = g.vy[oyl], r = w & 0xFFu;
+                const uint32_t acc = g.h[r][ox] * ((w >> 8) & 31u) + g.h[r + 1][ox] * ((w >> 13) & 31u) +
+                                     g.h[r + 2][ox] * ((w >> 18) & 31u) + g.h[r + 3][ox] * ((w >> 23) & 31u);
+                dst[(k * kG84Out + oyl) * kGray + ox] = (uint8_t)((acc + 640u) / 1280u);
+            }
         }
         __syncthreads();
     }

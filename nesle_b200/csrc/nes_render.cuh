@@ -74,9 +74,11 @@ NESLE_HD uint32_t rv_tile_entry(const RenderView& v, uint32_t y, uint32_t wx) {
     const uint32_t ntx = ((base & 1) + wx / 256) & 1;
     const uint32_t ntb = 0x2000 + (ntx | (nty << 1)) * 0x400;
     const uint32_t pb = (v.ctrl & 0x10) ? 0x1000 : 0;
-    const uint32_t tile = rv_mem(v, ntb + cy * 32 + cx);
-    const uint32_t lo = rv_mem(v, pb + tile * 16 + fy), hi = rv_mem(v, pb + tile * 16 + fy + 8);
-    const uint32_t at = rv_mem(v, ntb + 0x3C0 + (cy / 4) * 8 + cx / 4);
+    // Every address here is nametable space below $3000 or pattern space below
+    // $2000, so rv_mem's range dispatch reduces to these two reads.
+    const uint32_t tile = v.nt[mirror_nt(v.horizontal, ntb + cy * 32 + cx)];
+    const uint32_t lo = rv_chr(v, pb + tile * 16 + fy), hi = rv_chr(v, pb + tile * 16 + fy + 8);
+    const uint32_t at = v.nt[mirror_nt(v.horizontal, ntb + 0x3C0 + (cy / 4) * 8 + cx / 4)];
     const uint32_t group = (at >> (((cy & 2) << 1) | (cx & 2))) & 3;
     return lo | (hi << 8) | (group << 16);
 }
