@@ -97,3 +97,28 @@ def test_bench_reads_traffic_from_profile_summaries(summary):
 
     t = bench.profile_traffic(summary)
     assert t is not None and t > 1e8, summary
+
+
+def test_reference_arm_prints_one_contract_line():
+    """`bench.py --impl reference` (the reference CPU core on the host cores)
+    prints exactly one JSON line with the bench contract's keys, on CPU."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    from oracle import reference_available
+
+    if not reference_available():
+        pytest.skip("oracle/_ref not built")
+    root = Path(__file__).resolve().parents[1]
+    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--envs", "64", "--steps", "1",
+                          "--warmup", "1"], cwd=root, capture_output=True, text=True, timeout=300, check=True)
+    lines = [ln for ln in out.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["value"] > 0 and d["unit"] == "env-steps/s" and d["higher_is_better"]
+    assert d["metric"].startswith("env-steps/s") and d["n_gpus"] == 1 and d["steps"] == 1
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "reference" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
