@@ -137,3 +137,40 @@ def render_scroll_snapshots(seed: int, k: int) -> list[bytes]:
         s.oam = rng.integers(0, 256, 256, dtype=np.uint8).tobytes()
         out.append(w.write_fcs(s))
     return out
+
+
+# Controller protocol (batch_bus.cuh:105-133): reads with the strobe held high
+# (the live A bit, no shifting), then 12 reads after it drops (8 latched bits,
+# then 1s), and $4017 (constant $41 in the batched bus).  The loop is short and
+# its length depends on the A bit, so step boundaries land everywhere in it,
+# strobe high and mid-sequence included, at different points in different envs.
+def _controller_rom() -> bytes:
+    a = w.Asm(0x8000)
+    a.emit("LDA", w.IMM, 0x01)
+    a.emit("STA", w.ABS, 0x4016)
+    a.emit("LDA", w.ABS, 0x4016)
+    a.emit("STA", w.ZP, 0x10)
+    a.emit("LDA", w.ABS, 0x4016)
+    a.emit("STA", w.ZP, 0x11)
+    a.emit("AND", w.IMM, 0x01)
+    a.branch("BEQ", "even")
+    for _ in range(4):
+        a.emit("NOP")
+    a.label("even")
+    a.emit("LDA", w.IMM, 0x00)
+    a.emit("STA", w.ABS, 0x4016)
+    a.emit("LDX", w.IMM, 0x00)
+    a.label("rd")
+    a.emit("LDA", w.ABS, 0x4016)
+    a.emit("STA", w.ZPX, 0x20)
+    a.emit("INX")
+    a.emit("CPX", w.IMM, 0x0C)
+    a.branch("BNE", "rd")
+    a.emit("LDA", w.ABS, 0x4017)
+    a.emit("STA", w.ZP, 0x30)
+    a.emit("INC", w.ZP, 0x40)
+    a.emit("JMP", w.ABS, 0x8000)
+    return rom_with({0x8000: a.assemble()[0]})
+
+
+CONTROLLER_ROM = _controller_rom()

@@ -198,3 +198,19 @@ def test_render_scroll_split_matches_checker():
         for k in ("index", "rgb", "gray84"):
             np.testing.assert_array_equal(ro[k], rh[k], err_msg=k)
     assert (o.get("snap_sx_start") != o.get("snap_sx_end")).any()
+
+
+@pytest.mark.parametrize("cls", [HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreHybridStack])
+def test_controller_protocol_matches_checker(cls):
+    """Strobe-high reads, reads past the 8 latched bits and $4017, with step
+    boundaries at every point of the read sequence (the controller shift
+    register is one marker word inside a step, shift/count in the record)."""
+    n = 16
+    o = Oracle(n, 1, kat.CONTROLLER_ROM, [])
+    h = cls(n, 1, kat.CONTROLLER_ROM, [])
+    rng = np.random.default_rng(0)
+    for _ in range(12):
+        a = rng.integers(0, 256, n, dtype=np.uint8)
+        o.step(a, auto_reset=False)
+        h.step(a, auto_reset=False)
+        assert_same(o, h, label="controller")

@@ -305,3 +305,19 @@ def test_render_copy_matches_render_then_copy(n):
         _lib.check(g.lib.nesle_render_copy(g._h, mode, out.ctypes.data, out.nbytes, None))
         np.testing.assert_array_equal(out, want[key], err_msg=key)
         assert g.lib.nesle_render_copy(g._h, mode, out.ctypes.data, out.nbytes - 1, None) == _lib.NESLE_ERR_INVALID
+
+
+@pytest.mark.parametrize("variant", ["shared", "global", "hybrid", "hybrid-stack"])
+def test_controller_protocol_matches_checker(variant, monkeypatch):
+    """The controller known-answer ROM on every RAM placement: strobe-high reads,
+    reads past the 8 latched bits, $4017, step boundaries all through the reads."""
+    monkeypatch.setenv("NESLE_STEP_KERNEL", variant)
+    n = 64
+    o = Oracle(n, 1, kat.CONTROLLER_ROM, [])
+    g = GpuCore(n, 1, kat.CONTROLLER_ROM, [])
+    rng = np.random.default_rng(0)
+    for _ in range(12):
+        a = rng.integers(0, 256, n, dtype=np.uint8)
+        o.step(a, auto_reset=False)
+        g.step(a, auto_reset=False)
+        assert_same(o, g, label=f"controller {variant}")
