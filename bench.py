@@ -62,7 +62,11 @@ def parse_args(argv=None):
     ap.add_argument("--workload", default="config4", choices=["config4", "config3", "config2", "config1", "config5"])
     ap.add_argument("--obs", default="gray84", choices=["gray84", "rgb", "index"],
                     help="pixel mode (config3): the observation rendered every env-step")
+    ap.add_argument("--burn-in", type=int, default=None,
+                    help="untimed env-steps before the warm-up, so the timed region sees steady-state auto-resets "
+                         "(default 150 for config4, whose first frame-limit dones come at env-step 125; else 0)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-vecenv", action="store_true", help="skip the host VecEnv end-to-end figure")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args(argv)
 
@@ -259,6 +263,39 @@ def profile_traffic(summary: str = "step_kernel_config4.txt") -> float | None:
     return None
 
 
+def profile_figure(summary: str, key: str) -> float | None:
+    """A `key: value` line of a committed ncu summary (e.g. warp instructions per launch)."""
+    p = ROOT / "profiles" / summary
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        line = line.strip()
+        if line.startswith(key + ":"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def issue_roofline(instr: int, envs: int, kernel_ms: float, sm_mhz: float, summary: str | None) -> dict:
+    """Secondary roofline of the step kernel: warp-instruction issue.  The warp
+    instructions per launch come from the committed ncu summary of the same
+    workload (a count of the code, not a time); the rate uses the live kernel time."""
+    peak = 148 * 4 * sm_mhz * 1e6
+    out = {"emulated_instructions_per_s": instr / (kernel_ms / 1e3) if instr else None,
+           "emulated_instructions_per_env_step": instr / envs if instr else None,
+           "peak_warp_issue_per_s": peak, "unit": "warp instructions/s"}
+    warp = profile_figure(summary, "warp_instructions_per_launch") if summary else None
+    if warp:
+        out["warp_instructions_per_launch"] = warp
+        out["achieved"] = warp / (kernel_ms / 1e3)
+        out["issue_frac"] = out["achieved"] / peak
+        if instr:
+            out["warp_instructions_per_32_emulated_instructions"] = warp * 32 / instr
+    return out
+
+
 def shard(rank: int, envs_per_rank: int) -> tuple[int, np.ndarray]:
     """Global env range of one rank: [rank * n, (rank + 1) * n)."""
     offset = rank * envs_per_rank
@@ -301,7 +338,8 @@ def run_ours(args, rank, world, local) -> dict | None:
 
     batch = CudaBatch(n, wl.frameskip, wl.rom.image, *batch_snapshot_args(wl, env), device=local,
                       done_mode=wl.done_mode, done_args=wl.done_args, seed=wl.seed, env_offset=offset)
-    total_steps = args.warmup + args.steps
+    burn = args.burn_in
+    total_steps = burn + args.warmup + args.steps
     acts = torch.from_numpy(np.stack([wl.actions(env, s) for s in range(total_steps)])).to(dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -322,11 +360,14 @@ def run_ours(args, rank, world, local) -> dict | None:
         else:
             batch.render_device()
 
-    for s in range(args.warmup):
+    for s in range(burn):  # untimed: brings the frame-limit episodes to their first resets
+        device_step(s)
+    for s in range(burn, burn + args.warmup):
         device_step(s)
         if pixel:
             render_obs()
     torch.cuda.synchronize(dev)
+    episodes_before = int(batch.get_field("episode").astype(np.int64).sum())
     barrier()
     torch.cuda.synchronize(dev)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -335,7 +376,7 @@ def run_ours(args, rank, world, local) -> dict | None:
     instr = 0
     with ClockSampler(local) as clocks:
         time.sleep(0.3)  # let the sampler attach
-        for i, s in enumerate(range(args.warmup, total_steps)):
+        for i, s in enumerate(range(burn + args.warmup, total_steps)):
             starts[i].record(stream)
             device_step(s)
             mids[i].record(stream)
@@ -348,6 +389,7 @@ def run_ours(args, rank, world, local) -> dict | None:
     per_obs_ms = [a.elapsed_time(b) for a, b in zip(mids, ends)]
     elapsed_ms = starts[0].elapsed_time(ends[-1])
     instr = int(batch.get_field("stat_instructions").astype(np.int64).sum())  # last step only
+    resets = int(batch.get_field("episode").astype(np.int64).sum()) - episodes_before
     batch.synchronize()  # raises on illegal-opcode faults
 
     # e2e through the public host API with pinned host buffers
@@ -359,17 +401,36 @@ def run_ours(args, rank, world, local) -> dict | None:
         obs_kw = dict(render_frame=False, copy_obs=True, obs_mode=args.obs) if pixel else \
             dict(render_frame=False, copy_obs=False)
         out = None
-        for s in range(args.warmup):  # held like the timed loop holds it: the host buffers reach steady state
+        for s in range(burn, burn + args.warmup):  # held like the timed loop holds it: host buffers at steady state
             out = batch.step(host_np[s], **obs_kw)
         barrier()
         t0 = time.perf_counter()
-        for s in range(args.warmup, total_steps):
+        for s in range(burn + args.warmup, total_steps):
             out = batch.step(host_np[s], **obs_kw)
         e2e_s = time.perf_counter() - t0
         assert out["rewards"].shape == (n,)
         barrier()
 
+    # e2e through the host VecEnv (SB3 contract): RAM observations copied to the host every step
+    vec_s = None
+    if not args.no_e2e and not args.no_vecenv and not pixel:
+        from nesle_b200.vec_env import NesleVecEnv
+
+        vec = NesleVecEnv(None, n, wl.frameskip, action_masks=np.arange(256), observation_mode="ram", batch=batch)
+        host_idx = acts.cpu().numpy().astype(np.int64)
+        for s in range(burn, burn + args.warmup):
+            vec.step(host_idx[s])
+        barrier()
+        t0 = time.perf_counter()
+        for s in range(burn + args.warmup, total_steps):
+            obs, rew, dones, infos = vec.step(host_idx[s])
+        vec_s = time.perf_counter() - t0
+        assert obs.shape == (n, 2048) and len(infos) == n
+        barrier()
+        del vec
+
     elapsed_ms, e2e_s, instr = combine_over_ranks(elapsed_ms, e2e_s, instr, dev, world)
+    vec_s, _, resets = combine_over_ranks(vec_s or 0.0, None, resets, dev, world)
     clock_summary = clocks.summary()
 
     result = None
@@ -392,9 +453,10 @@ def run_ours(args, rank, world, local) -> dict | None:
             "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
             "config": workload_config(wl, n, world, args.obs),
             "roofline": step_roof,
-            "issue": {"emulated_instructions_per_s": instr / (kernel_ms / 1e3) if instr else None,
-                      "emulated_instructions_per_env_step": instr / (n * world) if instr else None,
-                      "peak_warp_issue_per_s": 148 * 4 * sm_mhz * 1e6},
+            "issue": issue_roofline(instr, n * world, kernel_ms, sm_mhz,
+                                    "step_kernel_config4.txt" if args.workload == "config4" else None),
+            "resets_in_timed_region": resets,
+            "burn_in_steps": burn,
             "kernel_ms": kernel_ms,
             "gpu_launches": args.steps * (2 if pixel else 1),
             "clocks": clock_summary,
@@ -417,6 +479,12 @@ def run_ours(args, rank, world, local) -> dict | None:
                              "path": (f"CudaBatch.step(pinned u8 actions, obs_mode='{args.obs}') -> obs, rewards, "
                                       "dones as numpy" if pixel else
                                       "CudaBatch.step(pinned u8 actions) -> rewards, dones as numpy")}
+        if vec_s:
+            result["e2e_host_obs"] = {
+                "value": total_env_steps / vec_s, "unit": UNIT, "h2d_bytes_per_step": 8 * n * world,
+                "d2h_bytes_per_step": (2048 + 5) * n * world,
+                "path": "NesleVecEnv(observation_mode='ram').step(action indices) -> RAM observations, rewards, "
+                        "dones and infos on the host (SB3 auto-reset contract)"}
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = reference_cpu_rate(wl, n, steps=2, warmup=1)
     if world > 1:
@@ -631,6 +699,8 @@ def main(argv=None) -> int:
     args = parse_args(argv)
     if args.envs is None:
         args.envs = 2048 if args.workload == "config5" else 65536
+    if args.burn_in is None:
+        args.burn_in = 150 if args.workload == "config4" else 0
     rank, world, local = dist_env()
     # Libraries (NCCL announces its version) may write to stdout; the result must
     # be the only line there, so fd 1 points at stderr until it is printed.

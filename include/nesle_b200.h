@@ -100,13 +100,19 @@ int nesle_render(nesle_batch* b, int mode, void* stream);
 
 /* No counterpart in the reference.  The 84x84 grey observation of every env
  * copied into `host_out` (num_envs * 7056 bytes), without allocating device
- * memory: the kernel renders into a static device scratch of 1,024 envs
- * (7,225,344 bytes, part of the library's module image) and the call copies
- * it out and synchronizes.  Batches of more than 1,024 envs are rejected
- * (NESLE_ERR_INVALID).  The scratch address is looked up once per device on
- * the first call: make that first call before any stream capture.  The
- * scratch is shared by all batches of a device, so concurrent calls race;
- * serialise them. */
+ * memory: for callers that cannot take a device allocation at call time, such
+ * as an evaluation or visualisation loop running beside a trainer whose
+ * caching allocator already holds the device's memory.  The kernel renders
+ * into a static device scratch of 1,024 envs (7,225,344 bytes, a global of the
+ * library's module).  The scratch is committed on a device, and its address
+ * looked up, by the first nesle_create on that device, so this call itself
+ * never asks the device for memory.  Batches of more than 1,024 envs are
+ * rejected (NESLE_ERR_INVALID).  The call copies the result out and
+ * synchronizes its stream before returning, so it must not be made while that
+ * stream is capturing.  The scratch is shared by all batches of a device, so
+ * calls that overlap on the GPU race; serialise them.  A device reset while
+ * the library is in use is not supported (the looked-up address would be
+ * stale). */
 int nesle_render_gray84_noalloc(nesle_batch* b, uint8_t* host_out, uint64_t bytes, void* stream);
 
 /* Env state save / restore; the device-side capture and restore of
@@ -118,7 +124,9 @@ int nesle_render_gray84_noalloc(nesle_batch* b, uint8_t* host_out, uint64_t byte
  * save copies envs[0..count) into count consecutive blobs at `dst`; load
  * writes blobs into envs (any env may receive any saved state).  Env lists
  * and blobs may be host or device memory; host indices are range-checked
- * (NESLE_ERR_INVALID), device indices past the batch are skipped.  With host
+ * (NESLE_ERR_INVALID); device indices past the batch are skipped without an
+ * error: on save their blobs keep whatever they held, on load nothing is
+ * written for them.  With host
  * blobs the call synchronises; with device blobs it is asynchronous on
  * `stream`.  The blob layout is this library's and can change with
  * nesle_abi_version().  Loaded blobs are taken as saved: a hand-edited

@@ -86,14 +86,19 @@ SIGNATURES = {
 }
 
 # EnvRecord (csrc/nesle_state.h), the first 128 bytes of a saved state blob.
-ENV_RECORD_DTYPE = np.dtype({
-    "names": ["pc", "a", "x", "y", "sp", "p", "nmi_pending", "cycles", "frame", "frame_dot", "ppu_ctrl",
-              "ppu_mask", "ppu_status", "oam_addr", "v", "t", "fine_x", "w", "open_bus", "read_buffer",
-              "scroll_x", "scroll_y", "prev_x", "prev_time", "episode", "status"],
-    "formats": ["<u2", "u1", "u1", "u1", "u1", "u1", "u1", "<u8", "<u8", "<u4", "u1", "u1", "u1", "u1", "<u2",
-                "<u2", "u1", "u1", "u1", "u1", "u1", "u1", "<i4", "<i4", "<u4", "<u4"],
-    "offsets": [0, 2, 3, 4, 5, 6, 7, 8, 16, 24, 28, 29, 30, 31, 32, 34, 36, 37, 38, 39, 40, 41, 56, 60, 68, 72],
-    "itemsize": 128})
+_REC = [("pc", "<u2", 0), ("a", "u1", 2), ("x", "u1", 3), ("y", "u1", 4), ("sp", "u1", 5), ("p", "u1", 6),
+        ("nmi_pending", "u1", 7), ("cycles", "<u8", 8), ("frame", "<u8", 16), ("frame_dot", "<u4", 24),
+        ("ppu_ctrl", "u1", 28), ("ppu_mask", "u1", 29), ("ppu_status", "u1", 30), ("oam_addr", "u1", 31),
+        ("v", "<u2", 32), ("t", "<u2", 34), ("fine_x", "u1", 36), ("w", "u1", 37), ("open_bus", "u1", 38),
+        ("read_buffer", "u1", 39), ("scroll_x", "u1", 40), ("scroll_y", "u1", 41), ("lat_sx", "u1", 42),
+        ("lat_sy", "u1", 43), ("lat_ctrl", "u1", 44), ("snap_sx_start", "u1", 45), ("snap_sy_start", "u1", 46),
+        ("snap_ctrl_start", "u1", 47), ("snap_sx_end", "u1", 48), ("snap_sy_end", "u1", 49),
+        ("snap_ctrl_end", "u1", 50), ("snap_mask", "u1", 51), ("ctrl_shift", "u1", 52), ("ctrl_count", "u1", 53),
+        ("ctrl_strobe", "u1", 54), ("flags", "u1", 55), ("prev_x", "<i4", 56), ("prev_time", "<i4", 60),
+        ("pending_dma", "<u4", 64), ("episode", "<u4", 68), ("status", "<u4", 72),
+        ("stat_instructions", "<u8", 80), ("stat_frames", "<u4", 88), ("stat_budget_hits", "<u4", 92)]
+ENV_RECORD_DTYPE = np.dtype({"names": [n for n, _, _ in _REC], "formats": [f for _, f, _ in _REC],
+                             "offsets": [o for _, _, o in _REC], "itemsize": 128})
 
 # Saved-state blob parts: name -> (offset, bytes); see nesle_save_states.
 STATE_PARTS = {"rec": (0, 128), "ram": (128, 2048), "prg_ram": (2176, 8192), "nametable": (10368, 2048),

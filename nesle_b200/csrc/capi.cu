@@ -112,14 +112,21 @@ struct nesle_batch {
     } while (0)
 
 // Static scratch of nesle_render_gray84_noalloc: 1,024 envs x 7,056 bytes
-// (7,225,344 B), part of the module image rather than a runtime allocation.
+// (7,225,344 B), a module global rather than a cudaMalloc.  Under lazy module
+// loading (the CUDA default) the module that holds it -- this file's, which has
+// no kernels -- is loaded, and the scratch committed on the device, by the
+// first cudaGetSymbolAddress.  nesle_create does that lookup, so the scratch
+// is committed while a batch is being allocated anyway, never later inside
+// the no-allocation call.  The cached address belongs to the device's current
+// context: resetting the device (cudaDeviceReset) while the library is in use
+// is not supported.
 constexpr uint32_t kNoAllocGrayEnvs = 1024;
 static __device__ __align__(256) uint8_t g_gray84_scratch[(size_t)kNoAllocGrayEnvs * kGray * kGray];
 constexpr int kNoAllocMaxDevices = 64;
 static std::mutex g_noalloc_mu;
 static uint8_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};
 
-// Address of the scratch on the current device (looked up once per device).
+// Address of the scratch on `device`, which must be current (looked up once per device).
 static int noalloc_scratch(int device, uint8_t** out) {
     if (device < 0 || device >= kNoAllocMaxDevices) return fail(NESLE_ERR_INVALID, "render_gray84_noalloc: device ordinal");
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
@@ -189,6 +196,8 @@ static int create_impl(const nesle_create_args* a, nesle_batch* b) {
     if (a->device < 0 || a->device >= ndev) return fail(NESLE_ERR_INVALID, "device ordinal out of range");
     DeviceGuard guard(a->device);
     CUDA_TRY(configure_kernels(), "configure kernels");
+    uint8_t* noalloc = nullptr;  // commits the no-allocation scratch now (see noalloc_scratch)
+    TRY(noalloc_scratch(a->device, &noalloc));
 
     const size_t n = b->n;
     BatchView& v = b->hv;
@@ -647,10 +656,12 @@ int nesle_fault_count(nesle_batch* b, uint32_t* count) {
 
 // No-allocation 84x84 observation: the render kernel writes into a file-scope
 // device scratch (module memory, set up once per device by
-// cudaGetSymbolAddress) and the result is copied to the caller's host buffer.
-// No cudaMalloc / cudaFree.  Concurrent calls on one device share the scratch
-// and race.  Every scratch byte the call reads is written by the kernel first,
-// so nothing needs clearing.
+// cudaGetSymbolAddress at nesle_create) and the result is copied to the
+// caller's host buffer.  No cudaMalloc / cudaFree.  Concurrent calls on one
+// device share the scratch and race.  Every scratch byte the call reads is
+// written by the kernel first, so nothing needs clearing.  The call ends with
+// a synchronisation of its stream, so it cannot be made while that stream is
+// capturing.
 int nesle_render_gray84_noalloc(nesle_batch* b, uint8_t* host_out, uint64_t bytes, void* stream) {
     if (!b || !host_out) return fail(NESLE_ERR_INVALID, "render_gray84_noalloc: null argument");
     if (b->n > kNoAllocGrayEnvs)
@@ -666,6 +677,7 @@ int nesle_render_gray84_noalloc(nesle_batch* b, uint8_t* host_out, uint64_t byte
     auto s = static_cast<cudaStream_t>(stream);
     CUDA_TRY(launch_render(b->dv, 0, b->n, scratch, NESLE_RENDER_GRAY84, s), "render_gray84_noalloc kernel");
     CUDA_TRY(cudaMemcpyAsync(host_out, scratch, bytes, cudaMemcpyDeviceToHost, s), "render_gray84_noalloc copy");
+    CUDA_TRY(cudaEventRecord(b->done_event, s), "record event");
     CUDA_TRY(cudaStreamSynchronize(s), "render_gray84_noalloc synchronize");
     return NESLE_OK;
 }

@@ -1,7 +1,10 @@
 // kernels.cu -- sm_100a kernels of the batched NES core.
 //
-//   step_kernel_global  one env-step per thread, env RAM in place (default)
+//   step_kernel_global  one env-step per thread, env RAM in place; with kHybrid
+//                   the zero page is staged in shared memory (the default
+//                   above two shared-memory waves, e.g. at 65,536 envs)
 //   step_kernel     one env-step per thread, env RAM staged in shared memory
+//                   (the default for small batches, e.g. 2,048 envs)
 //   reset_kernel    masked or full snapshot/cold reset
 //   poke_kernel     one RAM byte in every env
 //   render_kernel   colour-index or RGB frame from the presentation snapshot
@@ -21,8 +24,8 @@ __constant__ uint8_t kPaletteRgb[192] = NESLE_PALETTE_RGB;
 // --------------------------------------------------------------------------
 // Env step with RAM staged in shared memory.  One CTA = kStepSlots envs =
 // kStepSlots threads: 32 KB PRG + 8 KB execution entries + kStepSlots x 2 KB
-// interleaved RAM.  Kept as the alternative placement (NESLE_STEP_KERNEL=shared);
-// the in-place kernel below is the default.
+// interleaved RAM.  The default for batches of up to two waves of these CTAs
+// (NESLE_STEP_KERNEL=shared forces it); larger batches use the in-place kernel.
 // --------------------------------------------------------------------------
 constexpr uint32_t kPrgSmem = 32768 + 16;  // +16: the two-word fetch at $FFFC-$FFFD reads one word past the ROM
 constexpr uint32_t kDecSmem = 256 * sizeof(Entry);

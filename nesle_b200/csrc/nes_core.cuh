@@ -14,11 +14,15 @@
 // cuda/batch_bus.cuh, cuda/batch_ppu.cuh, cuda/batch_console.hpp,
 // cuda/batch_step.cuh); each function names the lines it follows.
 //
-// Memory: the env's 2 KB RAM lives in shared memory in a bank-interleaved
-// layout -- byte `a` of the env in slot `s` of a CTA with `S` slots is at
-// ((a & 0x7FC) * S + s * 4 + (a & 3)) -- so slot s always hits bank s % 32 and
-// no RAM access of a warp ever bank-conflicts.  PRG ROM (32 KB) and the decode
-// table are staged once per CTA into shared memory as well.
+// Memory: a Ctx says where the env's 2 KB RAM is for the launch.  Either the
+// whole row is staged in shared memory in a bank-interleaved layout -- byte
+// `a` of the env in slot `s` of a CTA with `S` slots is at
+// ((a & 0x7FC) * S + s * 4 + (a & 3)), so slot s always hits bank s % 32 and
+// no RAM access of a warp bank-conflicts (small batches) -- or the row stays
+// in place in global memory, optionally with one page (the zero page by
+// default) staged in an interleaved shared-memory slot (large batches, the
+// default at 65,536 envs).  PRG ROM (32 KB) and the execution entries are
+// staged once per CTA into shared memory in every placement.
 //
 // The header also compiles as plain C++ (NESLE_HD expands to nothing) so the
 // same code can be unit-tested on the CPU against the checker.

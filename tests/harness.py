@@ -180,6 +180,44 @@ class GpuCore(_Common):
     def _copy(self, name, out):
         _lib.check(self.lib.nesle_copy_field(self._h, name.encode(), out.ctypes.data, out.nbytes))
 
+    def gray84(self) -> np.ndarray:
+        """The 84x84 observations of every env (nesle_render + copy)."""
+        _lib.check(self.lib.nesle_render(self._h, _lib.RENDER_GRAY84, None))
+        return self.get("obs_gray84")
+
+    def window(self, envs) -> dict:
+        """Every state field of the listed envs, under the checker's field names,
+        through one nesle_save_states call (a few KB per env instead of whole-batch
+        copies)."""
+        idx = np.ascontiguousarray(envs, dtype=np.uint32)
+        blobs = np.zeros((len(idx), _lib.STATE_BYTES), np.uint8)
+        _lib.check(self.lib.nesle_save_states(self._h, idx.ctypes.data, len(idx), 0, blobs.ctypes.data, 0, None))
+        rec = blobs[:, :128].copy().view(_lib.ENV_RECORD_DTYPE).reshape(len(idx))
+        out = {name: rec[name].copy() for name in _lib.ENV_RECORD_DTYPE.names if name != "flags"}
+        checker_name = {v: k for k, v in PRODUCT_NAME.items()}
+        for part in ("ram", "prg_ram", "nametable", "palette", "oam", "snap_nametable", "snap_palette", "snap_oam"):
+            off, size = _lib.STATE_PARTS[part]
+            out[checker_name.get(part, part)] = blobs[:, off:off + size].copy()
+        off, _ = _lib.STATE_PARTS["out"]
+        f = blobs[:, off:off + 8].copy().view(np.float32)
+        out["reward"], out["last_reward"] = f[:, 0].copy(), f[:, 1].copy()
+        out["done"], out["last_done"] = blobs[:, off + 8].copy(), blobs[:, off + 9].copy()
+        return out
+
+
+def window_of(ref, fields=STATE_FIELDS) -> dict:
+    """The same dict from any core with get(field) (the checker)."""
+    return {f: ref.get(f) for f in fields}
+
+
+def assert_same_window(want: dict, got: dict, fields=STATE_FIELDS, label: str = "") -> None:
+    for f in fields:
+        a, b = want[f], got[f]
+        if not np.array_equal(a, b):
+            bad = np.nonzero((a != b).reshape(a.shape[0], -1).any(1))[0]
+            raise AssertionError(f"{label} field {f}: {len(bad)} envs differ, first {bad[:8].tolist()}; "
+                                 f"ref {a[bad[0]].ravel()[:16]} other {b[bad[0]].ravel()[:16]}")
+
 
 def assert_same(ref, other, fields=STATE_FIELDS, label: str = "") -> None:
     for f in fields:

@@ -1,11 +1,14 @@
-"""Multi-rank env sharding, on CPU over gloo (world_size 2).
+"""Multi-rank env sharding over gloo (world_size 2).
 
 Each rank owns the global env range that ``bench.shard`` gives it and builds
 its batch with ``env_offset``; snapshot levels, the frame-limit RNG and the
 action stream are keyed by the global env index.  Gathered over ranks, the
 sharded run must equal one batch over all envs, bit for bit -- the path has
-no exchange step, so nothing else couples the ranks.  The timing reduction
-``bench.combine_over_ranks`` is checked on the same process group.
+no exchange step, so nothing else couples the ranks.  Where CUDA exists each
+rank drives the product (libnesle_b200.so through its C ABI, on GPU
+rank % device_count) and the checker is only the comparison; without CUDA the
+ranks drive the checker, which still exercises the rank plumbing.  The timing
+reduction ``bench.combine_over_ranks`` is checked on the same process group.
 """
 from __future__ import annotations
 
@@ -28,18 +31,26 @@ def _short_config4():
     return wl
 
 
-def _run(wl, offset: int, n: int) -> dict:
-    from oracle import Oracle
-
+def _run(wl, offset: int, n: int, device: int | None = None) -> dict:
+    """The shard's state after STEPS env-steps: on the checker (device None) or
+    on the product on CUDA device `device`."""
     env = np.arange(offset, offset + n)
-    o = Oracle(n, wl.frameskip, wl.rom.image, wl.snapshots, env_to_level=wl.env_to_level(env),
-               done_mode=wl.done_mode, done_args=wl.done_args, seed=wl.seed, env_offset=offset)
+    kw = dict(env_to_level=wl.env_to_level(env), done_mode=wl.done_mode, done_args=wl.done_args, seed=wl.seed,
+              env_offset=offset)
+    if device is None:
+        from oracle import Oracle
+
+        o = Oracle(n, wl.frameskip, wl.rom.image, wl.snapshots, **kw)
+    else:
+        from harness import GpuCore
+
+        o = GpuCore(n, wl.frameskip, wl.rom.image, wl.snapshots, device=device, **kw)
     for s in range(STEPS):
         o.step(wl.actions(env, s))
     return {f: o.get(f) for f in FIELDS}
 
 
-def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
+def _worker(rank: int, world: int, port: int, result_dir: str, product: bool = False) -> None:
     import torch
     import torch.distributed as dist
 
@@ -51,7 +62,7 @@ def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
         wl = _short_config4()
         offset, env = bench.shard(rank, ENVS_PER_RANK)
         assert offset == rank * ENVS_PER_RANK and len(env) == ENVS_PER_RANK
-        mine = _run(wl, offset, ENVS_PER_RANK)
+        mine = _run(wl, offset, ENVS_PER_RANK, rank % torch.cuda.device_count() if product else None)
         gathered = [None] * world
         dist.all_gather_object(gathered, mine)
         # rank r reports elapsed 10 + r ms, e2e 1 + r s, 100 * (r + 1) instructions
@@ -78,6 +89,21 @@ def _free_port() -> int:
 def test_two_rank_sharding_equals_one_batch(tmp_path):
     mp = pytest.importorskip("torch.multiprocessing")
     mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    assert (tmp_path / "ok").read_text() == "ok"
+
+
+@pytest.mark.gpu
+def test_two_rank_sharding_on_the_product(tmp_path):
+    """The same over gloo with each rank stepping its shard on the CUDA path."""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from nesle_b200 import build
+
+    build.build()
+    mp = pytest.importorskip("torch.multiprocessing")
+    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path), True), nprocs=2, join=True,
+                       start_method="spawn")
     assert (tmp_path / "ok").read_text() == "ok"
 
 

@@ -51,6 +51,25 @@ def test_matches_allocating_render_on_two_calls_in_a_row(n):
     assert len(np.unique(ref)) > 8  # real frames, not a constant
 
 
+def test_first_call_on_a_fresh_batch_leaves_no_frame_buffer():
+    """On a batch that has never rendered, the no-allocation call works first
+    and leaves no observation buffer behind; the allocating render made
+    afterwards gives the same bytes."""
+    from harness import GpuCore
+
+    wl = w.config3()
+    n = 96
+    g = GpuCore(n, wl.frameskip, wl.rom.image, [], done_mode=wl.done_mode, done_args=wl.done_args, seed=wl.seed)
+    g.step(wl.actions(np.arange(n), 0))
+    out = np.full((n, 84, 84), 0x5A, np.uint8)
+    _lib.check(_noalloc(g, out))
+    probe = np.zeros((n, 84, 84), np.uint8)
+    rc = g.lib.nesle_copy_field(g._h, b"obs_gray84", probe.ctypes.data, probe.nbytes)
+    assert rc == _lib.NESLE_ERR_RUNTIME and b"not been rendered" in g.lib.nesle_last_error()
+    _lib.check(g.lib.nesle_render(g._h, _lib.RENDER_GRAY84, None))
+    np.testing.assert_array_equal(out, g.get("obs_gray84"))
+
+
 def test_rejects_batches_beyond_the_scratch_and_wrong_sizes():
     from harness import GpuCore
 
