@@ -198,7 +198,15 @@ int nesle_fault_count(nesle_batch* b, uint32_t* count);
 typedef struct nesle_info {
     uint32_t num_envs, frameskip, num_levels, device;
     uint32_t envs_per_block, smem_bytes_per_block;
+    uint32_t step_placement; /* where the step kernel keeps env RAM: NESLE_PLACEMENT_* */
 } nesle_info;
+
+#define NESLE_PLACEMENT_SHARED 0       /* whole RAM row staged in shared memory (small batches) */
+#define NESLE_PLACEMENT_GLOBAL 1       /* RAM row in place in device memory */
+#define NESLE_PLACEMENT_HYBRID 2       /* in place, zero page staged in shared memory */
+#define NESLE_PLACEMENT_HYBRID_STACK 3 /* in place, stack page staged in shared memory */
+#define NESLE_PLACEMENT_GLOBAL_ASYNC 4 /* in place, operands loaded ahead asynchronously */
+#define NESLE_PLACEMENT_HYBRID_ASYNC 5 /* hybrid, operands outside the zero page loaded ahead asynchronously */
 
 /* name / has_snapshot / num_levels properties (cuda_module.cu:947-957). */
 int nesle_get_info(nesle_batch* b, nesle_info* out);

@@ -446,15 +446,12 @@ class CudaBatch:
     @property
     def step_kernel_placement(self) -> str:
         """Where the step kernel keeps env RAM: "shared" (staged in shared memory),
-        "hybrid" (in place, zero page in shared memory) or "global" (in place)."""
+        "global" (in place), "hybrid" (in place, zero page in shared memory),
+        "hybrid-stack" (stack page instead), and the "-async" forms of the in-place
+        ones (operands loaded ahead asynchronously)."""
         info = _lib.Info()
         self._check(self._lib.nesle_get_info(self._h, ctypes.byref(info)))
-        staging = 32768 + 16 + 256 * 32  # PRG + execution entries
-        if info.smem_bytes_per_block == staging:
-            return "global"
-        if info.smem_bytes_per_block == staging + info.envs_per_block * 256:
-            return "hybrid"
-        return "shared"
+        return _lib.PLACEMENTS[info.step_placement]
 
     def frames_index_device(self, render: bool = True) -> CudaDeviceArrayView:
         if render:

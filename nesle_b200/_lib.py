@@ -35,7 +35,10 @@ class CreateArgs(ctypes.Structure):
 class Info(ctypes.Structure):
     _fields_ = [("num_envs", ctypes.c_uint32), ("frameskip", ctypes.c_uint32), ("num_levels", ctypes.c_uint32),
                 ("device", ctypes.c_uint32), ("envs_per_block", ctypes.c_uint32),
-                ("smem_bytes_per_block", ctypes.c_uint32)]
+                ("smem_bytes_per_block", ctypes.c_uint32), ("step_placement", ctypes.c_uint32)]
+
+
+PLACEMENTS = ("shared", "global", "hybrid", "hybrid-stack", "global-async", "hybrid-async")
 
 
 class FcsState(ctypes.Structure):

@@ -145,7 +145,7 @@ extern "C" {
 
 const char* nesle_last_error(void) { return g_err.c_str(); }
 
-int nesle_abi_version(void) { return 1; }
+int nesle_abi_version(void) { return 2; }
 
 int nesle_parse_fcs(const uint8_t* data, size_t len, nesle_fcs_state* out) {
     if (!data || !out) return fail(NESLE_ERR_INVALID, "parse_fcs: null argument");
@@ -316,6 +316,8 @@ static int create_impl(const nesle_create_args* a, nesle_batch* b) {
         else if (strcmp(sv, "shared") == 0) b->step_variant = kStepSharedRam;
         else if (strcmp(sv, "hybrid") == 0) b->step_variant = kStepHybridRam;
         else if (strcmp(sv, "hybrid-stack") == 0) b->step_variant = kStepHybridStackRam;
+        else if (strcmp(sv, "global-async") == 0) b->step_variant = kStepGlobalAsync;
+        else if (strcmp(sv, "hybrid-async") == 0) b->step_variant = kStepHybridAsync;
     }
     b->step_threads = global_step_threads(b->n, static_cast<uint32_t>(sms));
     CUDA_TRY(cudaEventCreateWithFlags(&b->done_event, cudaEventDisableTiming), "create event");
@@ -689,9 +691,10 @@ int nesle_get_info(nesle_batch* b, nesle_info* out) {
     out->num_levels = b->num_levels;
     out->device = static_cast<uint32_t>(b->device);
     out->envs_per_block = b->step_variant == kStepSharedRam ? kStepSlots : b->step_threads;
-    out->smem_bytes_per_block = b->step_variant == kStepSharedRam ? static_cast<uint32_t>(step_smem_bytes())
-                                : 32768 + 16 + 256 * 32 +
-                                      (b->step_variant >= kStepHybridRam ? b->step_threads * 256 : 0);
+    out->step_placement = b->step_variant;  // the kStep* values equal NESLE_PLACEMENT_*
+    out->smem_bytes_per_block = b->step_variant == kStepSharedRam
+                                    ? static_cast<uint32_t>(step_smem_bytes())
+                                    : static_cast<uint32_t>(global_step_smem(b->step_variant, b->step_threads));
     return NESLE_OK;
 }
 

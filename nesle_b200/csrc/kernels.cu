@@ -126,12 +126,55 @@ struct DeviceProfile {
     }
 };
 
+// Asynchronous operand load of one lane (run_frames_async): a 4-byte cp.async
+// from the env's RAM row into the lane's shared-memory word, completing on the
+// lane's own mbarrier (expected arrival count 1, so every load is one phase).
+// Readiness is tested without waiting (mbarrier.test_wait.parity).
+struct DeviceAsync {
+    uint32_t word_addr, bar_addr;  // shared-window addresses
+    __device__ __forceinline__ void init(uint32_t* word, unsigned long long* bar) {
+        word_addr = static_cast<uint32_t>(__cvta_generic_to_shared(word));
+        bar_addr = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_addr) : "memory");
+    }
+    __device__ __forceinline__ void issue(const uint8_t* src) {
+        asm volatile("cp.async.ca.shared::cta.global [%0], [%1], 4;" ::"r"(word_addr), "l"(src) : "memory");
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar_addr) : "memory");
+    }
+    __device__ __forceinline__ bool ready(uint32_t parity) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar_addr), "r"(parity)
+            : "memory");
+        return ok != 0;
+    }
+    __device__ __forceinline__ uint32_t word() const {
+        uint32_t w;
+        asm volatile("ld.shared::cta.u32 %0, [%1];" : "=r"(w) : "r"(word_addr) : "memory");
+        return w;
+    }
+    // A load still in flight when the lane stops (only after a stall): wait for
+    // it with the same bound, so nothing lands in shared memory after the CTA.
+    __device__ __forceinline__ void drain(uint32_t parity) {
+        for (uint32_t i = 0; i < kAsyncSpinLimit && !ready(parity); ++i) {
+        }
+    }
+};
+
+constexpr uint32_t kAsyncSmemPerLane = 12;  // mbarrier (8 B) + operand word (4 B)
+
 // kHybrid: each env's zero page ($0000-$00FF) is staged into shared memory for
 // the launch (interleaved 4 bytes per lane: every lane keeps to its own bank)
 // and written back before the env's done/auto-reset; the rest of RAM stays in
 // place.  Zero-page operands and indirect pointers then cost a shared-memory
 // access instead of a global one.
-template <bool kProfile, bool kHybrid>
+// kAsync: RAM operands outside the slot are loaded ahead asynchronously
+// (run_frames_async); the per-lane barriers and words follow the slots.
+template <bool kProfile, bool kHybrid, bool kAsync = false>
 __global__ void __launch_bounds__(kGlobalMaxThreads, 1)
 step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
                    const long long* __restrict__ act64, uint32_t flags, unsigned long long* __restrict__ prof_op,
@@ -141,6 +184,7 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
     uint8_t* s_prg = smem;
     Entry* s_dec = reinterpret_cast<Entry*>(smem + kPrgSmem);
     uint32_t* s_zp = reinterpret_cast<uint32_t*>(smem + kPrgSmem + kDecSmem);  // [64 words][blockDim lanes]
+    uint8_t* s_async = smem + kPrgSmem + kDecSmem + (kHybrid ? (size_t)blockDim.x * 256 : 0);
     const BatchView& v = *vp;
     const uint32_t tid = threadIdx.x;
     const uint4* prg_src = reinterpret_cast<const uint4*>(v.prg);
@@ -189,8 +233,16 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
         const uint8_t action = act64 ? (uint8_t)(act64[env] & 0xFF) : act8[env];
         float reward;
         uint8_t done;
-        if (kProfile) run_env_step<false>(c, rec, action, reward, done, DeviceProfile{s_op, prof_pc});
-        else run_env_step<false>(c, rec, action, reward, done);
+        if (kProfile) {
+            run_env_step<false>(c, rec, action, reward, done, DeviceProfile{s_op, prof_pc});
+        } else if (kAsync) {
+            DeviceAsync A;
+            A.init(reinterpret_cast<uint32_t*>(s_async + (size_t)blockDim.x * 8 + tid * 4),
+                   reinterpret_cast<unsigned long long*>(s_async + tid * 8));
+            run_env_step_async(c, rec, action, reward, done, A);
+        } else {
+            run_env_step<false>(c, rec, action, reward, done);
+        }
         if (kHybrid) {  // back in place before a possible auto-reset rewrites the row
             uint4* dst = reinterpret_cast<uint4*>(c.ram + slot_page);
 #pragma unroll 4
@@ -631,14 +683,23 @@ gray84_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint3
 // --------------------------------------------------------------------------
 size_t step_smem_bytes() { return kPrgSmem + kDecSmem + (size_t)kStepSlots * kRamBytes; }
 
-constexpr size_t kHybridSmemMax = kPrgSmem + kDecSmem + (size_t)kGlobalMaxThreads * 256;
+size_t global_step_smem(uint32_t variant, uint32_t threads) {
+    const bool hybrid = variant == kStepHybridRam || variant == kStepHybridStackRam || variant == kStepHybridAsync;
+    const bool async = variant == kStepGlobalAsync || variant == kStepHybridAsync;
+    return kPrgSmem + kDecSmem + (hybrid ? (size_t)threads * 256 : 0) + (async ? (size_t)threads * kAsyncSmemPerLane : 0);
+}
 
 cudaError_t configure_kernels() {
     cudaError_t e = cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)step_smem_bytes());
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(step_kernel_global<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kHybridSmemMax);
+                             (int)global_step_smem(kStepHybridRam, kGlobalMaxThreads));
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(step_kernel_global<false, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)global_step_smem(kStepHybridAsync, kGlobalMaxThreads));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(step_kernel_global<false, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)global_step_smem(kStepGlobalAsync, kGlobalMaxThreads));
     return e;
 }
 
@@ -663,12 +724,20 @@ cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* a
                                                                                     prof_pc, 0);
     } else if (variant == kStepGlobalRam) {
         const uint32_t blocks = (num_envs + threads - 1) / threads;
-        step_kernel_global<false, false><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags, nullptr,
-                                                                                      nullptr, 0);
+        step_kernel_global<false, false><<<blocks, threads, global_step_smem(variant, threads), s>>>(
+            dv, act8, act64, flags, nullptr, nullptr, 0);
     } else if (variant == kStepHybridRam || variant == kStepHybridStackRam) {
         const uint32_t blocks = (num_envs + threads - 1) / threads;
-        step_kernel_global<false, true><<<blocks, threads, kPrgSmem + kDecSmem + (size_t)threads * 256, s>>>(
+        step_kernel_global<false, true><<<blocks, threads, global_step_smem(variant, threads), s>>>(
             dv, act8, act64, flags, nullptr, nullptr, variant == kStepHybridStackRam ? 0x100u : 0u);
+    } else if (variant == kStepGlobalAsync) {
+        const uint32_t blocks = (num_envs + threads - 1) / threads;
+        step_kernel_global<false, false, true><<<blocks, threads, global_step_smem(variant, threads), s>>>(
+            dv, act8, act64, flags, nullptr, nullptr, 0);
+    } else if (variant == kStepHybridAsync) {
+        const uint32_t blocks = (num_envs + threads - 1) / threads;
+        step_kernel_global<false, true, true><<<blocks, threads, global_step_smem(variant, threads), s>>>(
+            dv, act8, act64, flags, nullptr, nullptr, 0);
     } else {
         const uint32_t blocks = (num_envs + kStepSlots - 1) / kStepSlots;
         step_kernel<<<blocks, kStepSlots, step_smem_bytes(), s>>>(dv, act8, act64, flags);

@@ -4,6 +4,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "../../include/nesle_b200.h"
 #include "nesle_state.h"
 
 namespace nesle {
@@ -11,7 +12,18 @@ namespace nesle {
 constexpr uint32_t kStepSlots = 64;       // envs (threads) per shared-RAM step CTA (multiple of 32: conflict-free banks)
 constexpr uint32_t kGlobalMaxThreads = 448;  // max envs (threads) per in-place step CTA
 
-enum : uint32_t { kStepSharedRam = 0, kStepGlobalRam = 1, kStepHybridRam = 2, kStepHybridStackRam = 3 };
+enum : uint32_t {
+    kStepSharedRam = 0,       // whole RAM row staged in shared memory
+    kStepGlobalRam = 1,       // RAM row in place
+    kStepHybridRam = 2,       // in place, zero page staged in a shared-memory slot
+    kStepHybridStackRam = 3,  // in place, stack page in the slot
+    kStepGlobalAsync = 4,     // in place, operands loaded ahead asynchronously
+    kStepHybridAsync = 5,     // hybrid, operands outside the slot loaded ahead asynchronously
+};
+static_assert(kStepSharedRam == NESLE_PLACEMENT_SHARED && kStepHybridAsync == NESLE_PLACEMENT_HYBRID_ASYNC,
+              "step variants are the ABI's placement codes");
+// Dynamic shared memory of one in-place step CTA of `threads` lanes.
+size_t global_step_smem(uint32_t variant, uint32_t threads);
 
 enum : uint32_t { kStepDeviceApi = 1, kStepAutoReset = 2 };
 

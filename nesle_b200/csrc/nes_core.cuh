@@ -858,12 +858,37 @@ NESLE_HD void fetch_bus(const Ctx& c, Lane& L, Fetched& f) {
 // kSharedRam: the env's RAM sits in the interleaved shared-memory slot;
 // otherwise it is the env's row in global memory and loads are predicated.
 // ---------------------------------------------------------------------------
+// Effective address of instruction `f` with the lane's current registers
+// (cpu.hpp:378-587 addressing modes); `page` gets the page-cross cycle.
+// Indirect pointers are read from RAM here (the zero-page slot in the hybrid
+// placement).
 template <bool kSharedRam>
-NESLE_HD uint32_t exec_uniform(const Ctx& c, Lane& L, Fetched& f, bool& fresh) {
+NESLE_HD uint32_t effective_address(const Ctx& c, const Lane& L, const Fetched& f, uint32_t& page) {
+    const uint32_t R = L.R, w0 = f.e.w[0], w1 = f.e.w[1];
+    const uint32_t b16 = f.b1 | (f.b2 << 8);
+    const uint32_t idx = (R >> byte_of(w1, 0)) & byte_of(w1, 1);
+    const uint32_t zp = (f.b1 + ((R >> 8) & byte_of(w1, 2))) & 0xFF;
+    const bool ind = (w0 & E1_IND) != 0;
+    uint32_t ptr = 0;
+    if (kSharedRam || ind) ptr = ram_rd(c, zp) | (ram_rd(c, (zp + 1) & 0xFF) << 8);
+    const uint32_t wrap = (w0 & E1_ZP) ? 0xFFu : 0xFFFFu;
+    const uint32_t base = ind ? ptr : (b16 & wrap);
+    const uint32_t addr = (base + idx) & wrap;
+    page = ((w0 & E0_PAGE) && ((base ^ addr) & 0xFF00u)) ? 1u : 0u;
+    return (w0 & E1_STACK) ? (0x100u | (((R >> 24) + ((w0 >> 9) & 1u)) & 0xFFu)) : addr;
+}
+
+// The instruction at effective address `addr` (page-cross cycle `page`).
+// kAsync: a RAM operand outside the zero-page slot was loaded ahead into
+// `async_word` (the aligned 4-byte word holding it) when `async_ready`.
+template <bool kSharedRam, bool kAsync>
+NESLE_HD uint32_t exec_at(const Ctx& c, Lane& L, Fetched& f, bool& fresh, uint32_t addr, uint32_t page,
+                          bool async_ready, uint32_t async_word) {
     const uint32_t pc = L.pc, b1 = f.b1, b2 = f.b2, R = L.R, P = L.p;
     const uint32_t w0 = f.e.w[0], w1 = f.e.w[1], w2 = f.e.w[2], w3 = f.e.w[3], w4 = f.e.w[4], w5 = f.e.w[5];
     const uint32_t wmask = f.e.w[6], spd = f.e.w[7];
     const uint32_t b16 = b1 | (b2 << 8);
+    (void)w1;
 
     // ---- next PC (flags from the previous instruction), then prefetch it ----
     const uint32_t seq = (pc + byte_of(w0, 2)) & 0xFFFF;
@@ -871,21 +896,9 @@ NESLE_HD uint32_t exec_uniform(const Ctx& c, Lane& L, Fetched& f, bool& fresh) {
     const bool taken = (P & byte_of(w5, 2)) == byte_of(w5, 3);
     uint32_t npc = taken ? target : seq;
     npc = (w0 & E0_JMP) ? b16 : npc;
-    uint32_t cyc = byte_of(w0, 3) + (taken ? 1u + (((seq ^ target) & 0xFF00u) ? 1u : 0u) : 0u);
+    uint32_t cyc = byte_of(w0, 3) + (taken ? 1u + (((seq ^ target) & 0xFF00u) ? 1u : 0u) : 0u) + page;
     Fetched nf;
     fetch_prg(c, npc, nf);
-
-    // ---- effective address ----
-    const uint32_t idx = (R >> byte_of(w1, 0)) & byte_of(w1, 1);
-    const uint32_t zp = (b1 + ((R >> 8) & byte_of(w1, 2))) & 0xFF;
-    const bool ind = (w0 & E1_IND) != 0;
-    uint32_t ptr = 0;
-    if (kSharedRam || ind) ptr = ram_rd(c, zp) | (ram_rd(c, (zp + 1) & 0xFF) << 8);
-    const uint32_t wrap = (w0 & E1_ZP) ? 0xFFu : 0xFFFFu;
-    const uint32_t base = ind ? ptr : (b16 & wrap);
-    uint32_t addr = (base + idx) & wrap;
-    cyc += ((w0 & E0_PAGE) && ((base ^ addr) & 0xFF00u)) ? 1u : 0u;
-    addr = (w0 & E1_STACK) ? (0x100u | (((R >> 24) + ((w0 >> 9) & 1u)) & 0xFFu)) : addr;
 
     // ---- operand read: RAM/PRG from fast memory, $4016/$4017 and the
     //      unmapped $4000-$5FFF reads inline, PPU registers and PRG-RAM aside ----
@@ -898,6 +911,9 @@ NESLE_HD uint32_t exec_uniform(const Ctx& c, Lane& L, Fetched& f, bool& fresh) {
     if (kSharedRam) {
         const uint8_t* src = is_ram ? ram_byte : c.prg + (addr & 0x7FFF);
         mem = *src;
+    } else if (kAsync) {
+        mem = c.prg[addr & 0x7FFF];
+        if (rd && is_ram) mem = async_ready ? (async_word >> ((addr & 3u) * 8u)) & 0xFFu : (uint32_t)*ram_byte;
     } else {
         mem = c.prg[addr & 0x7FFF];
         if (rd && is_ram) mem = *ram_byte;
@@ -948,6 +964,13 @@ NESLE_HD uint32_t exec_uniform(const Ctx& c, Lane& L, Fetched& f, bool& fresh) {
     // only a pending NMI, which a $2000 write can raise, needs the loop top.
     fresh = in_prg_window(npc) && !L.nmi;
     return cyc;
+}
+
+template <bool kSharedRam>
+NESLE_HD uint32_t exec_uniform(const Ctx& c, Lane& L, Fetched& f, bool& fresh) {
+    uint32_t page;
+    const uint32_t addr = effective_address<kSharedRam>(c, L, f, page);
+    return exec_at<kSharedRam, false>(c, L, f, fresh, addr, page, false, 0u);
 }
 
 // ---------------------------------------------------------------------------
@@ -1072,6 +1095,128 @@ NESLE_HD void run_frames(const Ctx& c, Lane& L, const Prof& prof = Prof()) {
         }
     }
 }
+
+// ---------------------------------------------------------------------------
+// Decoupled operand loads (in-place RAM placements).
+//
+// With RAM rows in global memory a warp's operand load waits for its slowest
+// lane, and a lane's RAM line is usually in L2 or DRAM, so every iteration of
+// the synchronous loop pays the worst latency of 32 lanes.  Here each lane
+// loads the operand of its *next* instruction as soon as its effective address
+// is known (at the end of the current instruction) with an asynchronous copy
+// into its own shared-memory word that completes on its own barrier.  At the
+// top of the next iteration the lane tests that barrier without waiting: a
+// lane whose operand has arrived executes, one whose operand is still in
+// flight sits the iteration out while the other lanes run.  The lanes of a warp
+// therefore no longer wait for each other's memory.
+//
+// Exactness: the load is issued after every store of the lane's earlier
+// instructions (program order), and between the issue and the use the lane
+// executes nothing.  Operands in the zero-page slot, PRG ROM, I/O space and
+// immediates are read when the instruction executes, as in run_frames.
+//
+// `Async` provides issue(src) / ready(parity) / word() / drain(); the device
+// implementation uses cp.async with a per-lane mbarrier (kernels.cu), the host
+// build copies at issue time and reports "not ready" on a pseudo-random third
+// of tests to exercise the idle path.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kAsyncSpinLimit = 1u << 22;  // idle iterations one operand may take before the lane stops
+
+// Effective address of `f`; issues its operand load when that operand is a
+// RAM byte outside the zero-page slot.  Returns whether a load was issued.
+template <class Async>
+NESLE_HD bool prepare_operand(const Ctx& c, const Lane& L, const Fetched& f, uint32_t& addr, uint32_t& page,
+                              Async& A) {
+    addr = effective_address<false>(c, L, f, page);
+    const uint32_t w0 = f.e.w[0];
+    const bool need = (w0 & E0_RD) && !(w0 & (E0_SPECIAL | E0_ILLEGAL)) && addr < 0x2000u && !in_zp_slot(c, addr);
+    if (need) A.issue(c.ram + (addr & 0x7FCu));
+    return need;
+}
+
+template <class Async>
+NESLE_HD void run_frames_async(const Ctx& c, Lane& L, Async& A) {
+    Fetched f{};
+    bool fresh = false;
+    bool pend = false;      // the current instruction's operand load is issued and not yet consumed
+    uint32_t parity = 0;    // phase of the lane's barrier that the pending load completes
+    uint32_t addr = 0, page = 0, pre_cyc = 0, spins = 0;
+    for (;;) {
+        if (!fresh || L.pending >= L.horizon || L.instr >= c.max_instr) {
+            if (!loop_top(c, L)) break;
+            if (L.nmi) {
+                L.nmi = 0;
+                nmi_entry(c, L);
+                pre_cyc = 7;
+                fresh = false;
+            }
+            if (!fresh) {
+                if (in_prg_window(L.pc)) fetch_prg(c, L.pc, f);
+                else fetch_bus(c, L, f);
+                fresh = true;
+            }
+            pend = prepare_operand(c, L, f, addr, page, A);
+        }
+        if (pend && !A.ready(parity)) {
+            if (++spins >= kAsyncSpinLimit) {  // stop the lane; the step reports it as faulted
+                L.status_word = NESLE_STATUS_STALL | addr;
+                fresh = false;
+            }
+            continue;
+        }
+        uint32_t word = 0;
+        if (pend) {
+            word = A.word();
+            parity ^= 1u;
+            spins = 0;
+        }
+        const uint32_t pc = L.pc, op = f.op;
+        uint32_t it_cyc = pre_cyc;
+        pre_cyc = 0;
+        if (f.e.w[0] & (E0_SPECIAL | E0_ILLEGAL)) {
+            if (f.e.w[0] & E0_ILLEGAL) {
+                // The reference executes `trap` (cpu.hpp:716-720); the env stops instead.
+                L.status_word = NESLE_STATUS_ILLEGAL | (op << 16) | pc;
+                L.cycles += it_cyc;
+                fresh = false;
+                pend = false;
+                continue;
+            }
+            exec_special(c, L, op, f.b1, f.b2);
+            it_cyc += byte_of(f.e.w[0], 3);
+            fresh = in_prg_window(L.pc) && !L.nmi;
+            if (fresh) fetch_prg(c, L.pc, f);
+        } else {
+            it_cyc += exec_at<false, true>(c, L, f, fresh, addr, page, pend, word);
+        }
+        pend = false;
+        it_cyc += L.dma;
+        L.dma = 0;
+        L.cycles += it_cyc;
+        L.pending += it_cyc * 3u;
+        L.instr++;
+        if (op == 0x4C && L.pc == pc) {  // JMP to itself (see run_frames)
+            idle_fast_forward(c, L);
+            fresh = false;
+        }
+        // The next instruction's operand, unless the next iteration starts at the loop top.
+        if (fresh && L.pending < L.horizon && L.instr < c.max_instr) pend = prepare_operand(c, L, f, addr, page, A);
+    }
+    if (pend) A.drain(parity);
+}
+
+// Host stand-in for the asynchronous operand load: the copy happens at issue
+// and a deterministic third of the readiness tests say "not yet".
+struct HostAsync {
+    uint32_t w = 0, state = 0x9E3779B9u;
+    NESLE_HD void issue(const uint8_t* src) { memcpy(&w, src, 4); }
+    NESLE_HD bool ready(uint32_t) {
+        state = state * 1664525u + 1013904223u;
+        return (state >> 30) != 0u;
+    }
+    NESLE_HD uint32_t word() const { return w; }
+    NESLE_HD void drain(uint32_t) {}
+};
 
 // ---------------------------------------------------------------------------
 // Reward and done: batch_step.cuh:41-106 plus the configuration predicates.
@@ -1219,6 +1364,18 @@ NESLE_HD void run_env_step(const Ctx& c, EnvRecord& rec, uint8_t action, float& 
     load_lane(L, rec, action);
     begin_step(L);
     run_frames<kSharedRam>(c, L, prof);
+    reward_done(c, L, reward, done);
+    store_lane(L, rec);
+}
+
+// The same with the RAM row in place and operands loaded ahead (run_frames_async).
+template <class Async>
+NESLE_HD void run_env_step_async(const Ctx& c, EnvRecord& rec, uint8_t action, float& reward, uint8_t& done,
+                                 Async& A) {
+    Lane L;
+    load_lane(L, rec, action);
+    begin_step(L);
+    run_frames_async(c, L, A);
     reward_done(c, L, reward, done);
     store_lane(L, rec);
 }

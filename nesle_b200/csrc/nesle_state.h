@@ -34,6 +34,7 @@ enum {
 
 // Status word (EnvRecord::status): 0 = healthy.
 #define NESLE_STATUS_ILLEGAL 0x80000000u   // bits 16-23 opcode, 0-15 address
+#define NESLE_STATUS_STALL 0x40000000u     // an operand load did not complete in time; bits 0-15 address
 
 typedef struct __attribute__((aligned(16))) EnvRecord {
     // CPU (cpp/include/nesle/cpu.hpp:31-40)

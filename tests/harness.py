@@ -133,6 +133,14 @@ class HostCoreHybridStack(HostCore):
     global_ram = 3  # in place, stack page in a separate slot
 
 
+class HostCoreGlobalAsync(HostCore):
+    global_ram = 4  # in place, operands loaded ahead (with idle iterations)
+
+
+class HostCoreHybridAsync(HostCore):
+    global_ram = 5  # hybrid, operands outside the zero page loaded ahead
+
+
 class GpuCore(_Common):
     """libnesle_b200.so through its C ABI (host arrays in, host copies out)."""
 

@@ -33,6 +33,7 @@ struct HostBatch {
     uint32_t fault = 0;
     bool global_ram = false;  // run the in-place (global-RAM) variant of the core
     bool hybrid = false;      // ... with one page in a separate slot (hybrid placement)
+    bool async = false;       // ... with operands loaded ahead (run_frames_async, HostAsync)
     uint32_t slot_page = 0;   // the slot's page: 0x000 or 0x100
     std::vector<uint8_t> smem_ram = std::vector<uint8_t>(kSlots * kRamBytes);
 };
@@ -116,8 +117,11 @@ void host_destroy(void* p) { delete static_cast<HostBatch*>(p); }
 
 void host_set_global_ram(void* p, int on) {
     auto* h = static_cast<HostBatch*>(p);
-    h->global_ram = on != 0;  // 1 in place, 2 (3) in place with the zero page (stack page) in a separate slot
-    h->hybrid = on >= 2;
+    // 1 in place, 2 (3) in place with the zero page (stack page) in a separate slot,
+    // 4 (5) in place (hybrid) with operands loaded ahead
+    h->global_ram = on != 0;
+    h->hybrid = on == 2 || on == 3 || on == 5;
+    h->async = on == 4 || on == 5;
     h->slot_page = on == 3 ? 0x100u : 0u;
 }
 
@@ -182,7 +186,13 @@ void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) 
         float reward;
         uint8_t done;
         if (h->global_ram) {
-            run_env_step<false>(c, rec, actions[e], reward, done);
+            if (h->async) {
+                HostAsync A;
+                A.state ^= e * 0x85EBCA6Bu;  // a different idle pattern per env
+                run_env_step_async(c, rec, actions[e], reward, done, A);
+            } else {
+                run_env_step<false>(c, rec, actions[e], reward, done);
+            }
             if (h->hybrid) memcpy(h->ram.data() + (size_t)e * kRamBytes + c.zpage, zp, 256);
         } else {
             run_env_step<true>(c, rec, actions[e], reward, done);

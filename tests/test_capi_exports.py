@@ -45,7 +45,7 @@ def test_ctypes_binding_covers_the_header(lib_path):
     lib = _lib.load()
     for name in _lib.SIGNATURES:
         assert isinstance(getattr(lib, name), ctypes._CFuncPtr)
-    assert lib.nesle_abi_version() == 1
+    assert lib.nesle_abi_version() == 2
 
 
 def test_cpu_only_entry_points(lib_path):

@@ -6,16 +6,19 @@ import numpy as np
 import pytest
 
 import kat_roms as kat
-from harness import (STATE_FIELDS, HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreHybridStack, assert_same,
-                     run_lockstep)
+from harness import (STATE_FIELDS, HostCore, HostCoreGlobal, HostCoreGlobalAsync, HostCoreHybrid,
+                     HostCoreHybridAsync, HostCoreHybridStack, assert_same, run_lockstep)
 from nesle_b200 import workloads as w
 from oracle import Oracle
+
+# Every RAM placement of the step kernel, each compiled for the CPU.
+ALL_CORES = [HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreHybridStack, HostCoreGlobalAsync, HostCoreHybridAsync]
 
 
 @pytest.mark.parametrize("make,auto_reset", [(w.config1, False), (w.config2, True), (w.config3, True),
                                              (w.config4, True)])
 def test_configs_lockstep(make, auto_reset):
-    run_lockstep(make, 8, 8, auto_reset, [HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreHybridStack])
+    run_lockstep(make, 8, 8, auto_reset, ALL_CORES)
 
 
 def test_config3_frames_match_checker_every_step():
@@ -41,7 +44,7 @@ def test_frame_limit_auto_reset_lockstep():
         wl = w.config4()
         wl.done_args = (5, 17)
         return wl
-    _, _, dones = run_lockstep(short, 12, 20, True, [HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreHybridStack])
+    _, _, dones = run_lockstep(short, 12, 20, True, ALL_CORES)
     assert dones > 10
 
 
@@ -55,7 +58,7 @@ def test_smb_done_auto_reset_every_step():
     (kat.LDA_TAX_INX_STA, []), (kat.JSR_RTS, []), (kat.BNE_PAGE_CROSS, []), (kat.SEC_SBC, []),
     (kat.NMI_ROM, []), (kat.DMA_ROM, [kat.dma_snapshot()]), (kat.DMA_ZP_ROM, [kat.dma_zp_snapshot()]),
     (kat.IDLE_ROM, [])])
-@pytest.mark.parametrize("core", [HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreHybridStack])
+@pytest.mark.parametrize("core", ALL_CORES)
 def test_known_answer_roms(rom, snaps, core):
     o = Oracle(2, 2, rom, snaps)
     h = core(2, 2, rom, snaps)
@@ -100,8 +103,7 @@ def test_every_official_opcode_from_random_state(seed):
     """Each official opcode once from a random register/flag/RAM state (P bit 5 may be clear)."""
     for opc, rom, snap in _single_instruction_cases(seed, 1):
         o = Oracle(1, 1, rom, [snap])
-        sims = [HostCore(1, 1, rom, [snap]), HostCoreGlobal(1, 1, rom, [snap]), HostCoreHybrid(1, 1, rom, [snap]),
-                HostCoreHybridStack(1, 1, rom, [snap])]
+        sims = [cls(1, 1, rom, [snap]) for cls in ALL_CORES]
         a = np.zeros(1, np.uint8)
         o.step(a, auto_reset=False)
         for h in sims:
@@ -200,7 +202,7 @@ def test_render_scroll_split_matches_checker():
     assert (o.get("snap_sx_start") != o.get("snap_sx_end")).any()
 
 
-@pytest.mark.parametrize("cls", [HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreHybridStack])
+@pytest.mark.parametrize("cls", ALL_CORES)
 def test_controller_protocol_matches_checker(cls):
     """Strobe-high reads, reads past the 8 latched bits and $4017, with step
     boundaries at every point of the read sequence (the controller shift

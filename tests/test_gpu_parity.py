@@ -18,6 +18,9 @@ from oracle import Oracle
 
 pytestmark = pytest.mark.gpu
 
+# Every RAM placement of the step kernel (NESLE_STEP_KERNEL).
+PLACEMENTS = ["shared", "global", "hybrid", "hybrid-stack", "global-async", "hybrid-async"]
+
 
 @pytest.fixture(scope="module", autouse=True)
 def _cuda():
@@ -30,7 +33,7 @@ def _cuda():
 
 @pytest.mark.parametrize("make,auto_reset,n", [(w.config1, False, 64), (w.config2, True, 200),
                                                (w.config3, True, 200), (w.config4, True, 200)])
-@pytest.mark.parametrize("variant", ["shared", "global", "hybrid", "hybrid-stack"])
+@pytest.mark.parametrize("variant", PLACEMENTS)
 def test_configs_lockstep(make, auto_reset, n, variant, monkeypatch):
     """Every step, every field, against the checker (200 envs = 2 full CTAs + a partial one),
     for both placements of env RAM in the step kernel."""
@@ -56,7 +59,7 @@ def test_frame_limit_auto_reset_many_episodes():
     (kat.LDA_TAX_INX_STA, []), (kat.JSR_RTS, []), (kat.BNE_PAGE_CROSS, []), (kat.SEC_SBC, []),
     (kat.NMI_ROM, []), (kat.DMA_ROM, [kat.dma_snapshot()]), (kat.DMA_ZP_ROM, [kat.dma_zp_snapshot()]),
     (kat.IDLE_ROM, [])])
-@pytest.mark.parametrize("variant", ["shared", "global", "hybrid", "hybrid-stack"])
+@pytest.mark.parametrize("variant", PLACEMENTS)
 def test_known_answer_roms(rom, snaps, variant, monkeypatch):
     monkeypatch.setenv("NESLE_STEP_KERNEL", variant)
     o = Oracle(3, 2, rom, snaps)
@@ -307,7 +310,7 @@ def test_render_copy_matches_render_then_copy(n):
         assert g.lib.nesle_render_copy(g._h, mode, out.ctypes.data, out.nbytes - 1, None) == _lib.NESLE_ERR_INVALID
 
 
-@pytest.mark.parametrize("variant", ["shared", "global", "hybrid", "hybrid-stack"])
+@pytest.mark.parametrize("variant", PLACEMENTS)
 def test_controller_protocol_matches_checker(variant, monkeypatch):
     """The controller known-answer ROM on every RAM placement: strobe-high reads,
     reads past the 8 latched bits, $4017, step boundaries all through the reads."""
