@@ -207,6 +207,11 @@ typedef struct nesle_info {
 #define NESLE_PLACEMENT_HYBRID_STACK 3 /* in place, stack page staged in shared memory */
 #define NESLE_PLACEMENT_GLOBAL_ASYNC 4 /* in place, operands loaded ahead asynchronously */
 #define NESLE_PLACEMENT_HYBRID_ASYNC 5 /* hybrid, operands outside the zero page loaded ahead asynchronously */
+#define NESLE_PLACEMENT_INTERLEAVED 6  /* hybrid, the rest of RAM env-interleaved in a device working copy */
+#define NESLE_PLACEMENT_INTERLEAVED_ASYNC 7 /* the same with operands loaded ahead asynchronously */
+#define NESLE_PLACEMENT_GLOBAL_PRELOAD 8   /* in place, operands loaded one instruction ahead into registers */
+#define NESLE_PLACEMENT_HYBRID_PRELOAD 9   /* hybrid, the same for operands outside the zero page */
+#define NESLE_PLACEMENT_INTERLEAVED_PRELOAD 10 /* interleaved, the same */
 
 /* name / has_snapshot / num_levels properties (cuda_module.cu:947-957). */
 int nesle_get_info(nesle_batch* b, nesle_info* out);

@@ -38,7 +38,8 @@ class Info(ctypes.Structure):
                 ("smem_bytes_per_block", ctypes.c_uint32), ("step_placement", ctypes.c_uint32)]
 
 
-PLACEMENTS = ("shared", "global", "hybrid", "hybrid-stack", "global-async", "hybrid-async")
+PLACEMENTS = ("shared", "global", "hybrid", "hybrid-stack", "global-async", "hybrid-async", "interleaved",
+              "interleaved-async", "global-preload", "hybrid-preload", "interleaved-preload")
 
 
 class FcsState(ctypes.Structure):

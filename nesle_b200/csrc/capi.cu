@@ -318,8 +318,18 @@ static int create_impl(const nesle_create_args* a, nesle_batch* b) {
         else if (strcmp(sv, "hybrid-stack") == 0) b->step_variant = kStepHybridStackRam;
         else if (strcmp(sv, "global-async") == 0) b->step_variant = kStepGlobalAsync;
         else if (strcmp(sv, "hybrid-async") == 0) b->step_variant = kStepHybridAsync;
+        else if (strcmp(sv, "interleaved") == 0) b->step_variant = kStepInterleaved;
+        else if (strcmp(sv, "interleaved-async") == 0) b->step_variant = kStepInterleavedAsync;
+        else if (strcmp(sv, "global-preload") == 0) b->step_variant = kStepGlobalPreload;
+        else if (strcmp(sv, "hybrid-preload") == 0) b->step_variant = kStepHybridPreload;
+        else if (strcmp(sv, "interleaved-preload") == 0) b->step_variant = kStepInterleavedPreload;
     }
     b->step_threads = global_step_threads(b->n, static_cast<uint32_t>(sms));
+    if (step_interleaved(b->step_variant)) {  // the interleaved working copy: one 2 KB word column per lane
+        const size_t blocks = (b->n + b->step_threads - 1) / b->step_threads;
+        TRY(b->alloc(&v.ram_work, blocks * b->step_threads * kRamBytes, "interleaved ram"));
+        CUDA_TRY(cudaMemcpy(b->dv, &v, sizeof(BatchView), cudaMemcpyHostToDevice), "batch view upload");
+    }
     CUDA_TRY(cudaEventCreateWithFlags(&b->done_event, cudaEventDisableTiming), "create event");
     CUDA_TRY(launch_reset(b->dv, b->n, nullptr, true, nullptr), "initial reset");
     CUDA_TRY(cudaEventRecord(b->done_event, nullptr), "record event");

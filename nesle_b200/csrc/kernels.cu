@@ -132,12 +132,15 @@ struct DeviceProfile {
 // Readiness is tested without waiting (mbarrier.test_wait.parity).
 struct DeviceAsync {
     uint32_t word_addr, bar_addr;  // shared-window addresses
+    uint32_t shift = 0;            // bit position of the operand in the loaded word
     __device__ __forceinline__ void init(uint32_t* word, unsigned long long* bar) {
         word_addr = static_cast<uint32_t>(__cvta_generic_to_shared(word));
         bar_addr = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_addr) : "memory");
     }
-    __device__ __forceinline__ void issue(const uint8_t* src) {
+    __device__ __forceinline__ void issue(const uint8_t* byte_addr) {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(byte_addr) & ~(uintptr_t)3);
+        shift = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(byte_addr) & 3u) * 8u;
         asm volatile("cp.async.ca.shared::cta.global [%0], [%1], 4;" ::"r"(word_addr), "l"(src) : "memory");
         asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar_addr) : "memory");
     }
@@ -152,10 +155,10 @@ struct DeviceAsync {
             : "memory");
         return ok != 0;
     }
-    __device__ __forceinline__ uint32_t word() const {
+    __device__ __forceinline__ uint32_t byte() const {
         uint32_t w;
         asm volatile("ld.shared::cta.u32 %0, [%1];" : "=r"(w) : "r"(word_addr) : "memory");
-        return w;
+        return (w >> shift) & 0xFFu;
     }
     // A load still in flight when the lane stops (only after a stall): wait for
     // it with the same bound, so nothing lands in shared memory after the CTA.
@@ -167,14 +170,35 @@ struct DeviceAsync {
 
 constexpr uint32_t kAsyncSmemPerLane = 12;  // mbarrier (8 B) + operand word (4 B)
 
+// The operand of the next instruction as a plain global byte load into a
+// register, issued at the end of the current iteration (run_frames_async with
+// ready() always true).  The asm keeps the load where it is issued: the
+// compiler would otherwise move it down to its first use, and its "memory"
+// clobber keeps every earlier store of the lane ahead of it.
+struct DevicePreload {
+    uint32_t v = 0;
+    __device__ __forceinline__ void issue(const uint8_t* byte_addr) {
+        asm volatile("ld.global.u8 %0, [%1];" : "=r"(v) : "l"(byte_addr) : "memory");
+    }
+    __device__ __forceinline__ bool ready(uint32_t) const { return true; }
+    __device__ __forceinline__ uint32_t byte() const { return v; }
+    __device__ __forceinline__ void drain(uint32_t) const {}
+};
+
 // kHybrid: each env's zero page ($0000-$00FF) is staged into shared memory for
 // the launch (interleaved 4 bytes per lane: every lane keeps to its own bank)
 // and written back before the env's done/auto-reset; the rest of RAM stays in
 // place.  Zero-page operands and indirect pointers then cost a shared-memory
 // access instead of a global one.
-// kAsync: RAM operands outside the slot are loaded ahead asynchronously
-// (run_frames_async); the per-lane barriers and words follow the slots.
-template <bool kProfile, bool kHybrid, bool kAsync = false>
+// kOperand: 0 operands read when the instruction executes; 1 RAM operands
+// outside the slot loaded ahead with cp.async and per-lane barriers (which
+// follow the slots in shared memory); 2 loaded ahead into a register.
+// kInterleave: for the launch, RAM outside the slot moves to an env-interleaved
+// working copy in device memory (BatchView::ram_work: per CTA, word w of lane
+// l at (w * lanes + l) * 4), so the same address of the 32 envs of a warp is
+// one 128-byte line instead of 32 rows; copied in at the start and back at the
+// end of the launch.
+template <bool kProfile, bool kHybrid, int kOperand = 0, bool kInterleave = false>
 __global__ void __launch_bounds__(kGlobalMaxThreads, 1)
 step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
                    const long long* __restrict__ act64, uint32_t flags, unsigned long long* __restrict__ prof_op,
@@ -184,7 +208,7 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
     uint8_t* s_prg = smem;
     Entry* s_dec = reinterpret_cast<Entry*>(smem + kPrgSmem);
     uint32_t* s_zp = reinterpret_cast<uint32_t*>(smem + kPrgSmem + kDecSmem);  // [64 words][blockDim lanes]
-    uint8_t* s_async = smem + kPrgSmem + kDecSmem + (kHybrid ? (size_t)blockDim.x * 256 : 0);
+    uint8_t* s_async = smem + kPrgSmem + kDecSmem + (kHybrid ? (size_t)blockDim.x * 256 : 0);  // kOperand == 1
     const BatchView& v = *vp;
     const uint32_t tid = threadIdx.x;
     const uint4* prg_src = reinterpret_cast<const uint4*>(v.prg);
@@ -217,6 +241,21 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
             c.zslots = blockDim.x;
             c.zpage = slot_page;
         }
+        uint32_t* work = nullptr;
+        if (kInterleave) {
+            work = reinterpret_cast<uint32_t*>(v.ram_work + (size_t)blockIdx.x * blockDim.x * kRamBytes) + tid;
+            const uint4* src = reinterpret_cast<const uint4*>(c.ram);
+#pragma unroll 4
+            for (uint32_t q = 0; q < kRamBytes / 16; ++q) {
+                const uint4 w = src[q];
+                work[(4 * q + 0) * blockDim.x] = w.x;
+                work[(4 * q + 1) * blockDim.x] = w.y;
+                work[(4 * q + 2) * blockDim.x] = w.z;
+                work[(4 * q + 3) * blockDim.x] = w.w;
+            }
+            c.ram = reinterpret_cast<uint8_t*>(work);
+            c.slots = blockDim.x;
+        }
         c.prg = s_prg;
         c.dec = s_dec;
         c.view = vp;
@@ -235,16 +274,27 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
         uint8_t done;
         if (kProfile) {
             run_env_step<false>(c, rec, action, reward, done, DeviceProfile{s_op, prof_pc});
-        } else if (kAsync) {
+        } else if (kOperand == 1) {
             DeviceAsync A;
             A.init(reinterpret_cast<uint32_t*>(s_async + (size_t)blockDim.x * 8 + tid * 4),
                    reinterpret_cast<unsigned long long*>(s_async + tid * 8));
             run_env_step_async(c, rec, action, reward, done, A);
+        } else if (kOperand == 2) {
+            DevicePreload A;
+            run_env_step_async(c, rec, action, reward, done, A);
         } else {
             run_env_step<false>(c, rec, action, reward, done);
         }
+        uint8_t* row = v.ram + (size_t)env * kRamBytes;
+        if (kInterleave) {  // back in place first; the slot's page is written over it below
+            uint4* dst = reinterpret_cast<uint4*>(row);
+#pragma unroll 4
+            for (uint32_t q = 0; q < kRamBytes / 16; ++q)
+                dst[q] = make_uint4(work[(4 * q + 0) * blockDim.x], work[(4 * q + 1) * blockDim.x],
+                                    work[(4 * q + 2) * blockDim.x], work[(4 * q + 3) * blockDim.x]);
+        }
         if (kHybrid) {  // back in place before a possible auto-reset rewrites the row
-            uint4* dst = reinterpret_cast<uint4*>(c.ram + slot_page);
+            uint4* dst = reinterpret_cast<uint4*>(row + slot_page);
 #pragma unroll 4
             for (uint32_t q = 0; q < 16; ++q)
                 dst[q] = make_uint4(s_zp[(4 * q + 0) * blockDim.x + tid], s_zp[(4 * q + 1) * blockDim.x + tid],
@@ -599,7 +649,8 @@ render_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint3
 }
 
 // 84x84 grey observation, one CTA per env, on the same staged snapshot, in 6
-// strips of 40 source rows (exactly 14 output rows each):
+// strips of 40 source rows (exactly 14 output rows each), assembled in shared
+// memory and written out with one bulk copy per two strips:
 //   1. the strip as luma (render_strip with the palette groups in luma);
 //   2. horizontal area sums: output column ox covers source columns
 //      64 ox / 21 .. + 3 with weights in units of 1/21 px;
@@ -608,8 +659,13 @@ render_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint3
 // Nothing but the 7,056-byte observation is written to global memory.
 constexpr uint32_t kG84Rows = 40, kG84Out = 14;
 static_assert(kFrameH % kG84Rows == 0 && kG84Rows * kGray == kG84Out * kFrameH, "strip geometry");
+static_assert((2 * 14 * kGray) % 16 == 0 && (kGray * kGray) % 16 == 0,
+              "bulk copies move multiples of 16 bytes to 16-byte aligned rows");
+
+constexpr uint32_t kG84PairBytes = 2 * kG84Out * kGray;  // output rows of two strips: 2,352 B
 
 struct Gray84Smem {
+    __align__(16) uint8_t obs[kG84PairBytes];  // two strips of the observation, written out by one bulk copy
     uint32_t tiles[kG84Rows * kRowTiles];
     __align__(16) uint8_t luma[kG84Rows * kFrameW];
     uint16_t h[kG84Rows + 1][kGray];  // + a zero row read with weight 0
@@ -664,6 +720,9 @@ gray84_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint3
                 g.h[r][ox] = (uint16_t)(q[0] * w0 + q[1] * w1 + q[2] * w2 + q[3] * w3);
             }
         }
+        // The previous pair's bulk copy has read the buffer (issued a strip ago,
+        // so this wait is normally already satisfied) before it is written again.
+        if (tid == 0 && (k & 1u) == 0 && k > 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         __syncthreads();
         if (tid < 3 * kGray) {
             const uint32_t ox = tid % kGray;
@@ -671,11 +730,24 @@ gray84_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint3
                 const uint32_t w = g.vy[oyl], r = w & 0xFFu;
                 const uint32_t acc = g.h[r][ox] * ((w >> 8) & 31u) + g.h[r + 1][ox] * ((w >> 13) & 31u) +
                                      g.h[r + 2][ox] * ((w >> 18) & 31u) + g.h[r + 3][ox] * ((w >> 23) & 31u);
-                dst[(k * kG84Out + oyl) * kGray + ox] = (uint8_t)((acc + 640u) / 1280u);
+                g.obs[((k & 1u) * kG84Out + oyl) * kGray + ox] = (uint8_t)((acc + 640u) / 1280u);
             }
         }
+        // Every second strip, the pair's 2,352 bytes leave shared memory as one
+        // bulk copy (TMA engine, no multicast): each thread fences its writes for
+        // the async proxy, the barrier collects them, one thread issues the copy.
+        if (k & 1u) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
+        if ((k & 1u) && tid == 0) {
+            const uint32_t src = static_cast<uint32_t>(__cvta_generic_to_shared(g.obs));
+            asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst + (k / 2) * kG84PairBytes),
+                         "r"(src), "r"(kG84PairBytes)
+                         : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
     }
+    // The CTA's shared memory must outlive the last copy's read of it.
+    if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 // --------------------------------------------------------------------------
@@ -683,23 +755,61 @@ gray84_kernel(const BatchView* __restrict__ vp, uint8_t* __restrict__ out, uint3
 // --------------------------------------------------------------------------
 size_t step_smem_bytes() { return kPrgSmem + kDecSmem + (size_t)kStepSlots * kRamBytes; }
 
+// In-place step placements: (zero-page slot, operand mode, interleaved copy).
+struct GlobalPlacement {
+    bool hybrid;
+    int operand;  // 0 read at execution, 1 cp.async ahead, 2 register load ahead
+    bool interleave;
+};
+constexpr GlobalPlacement global_placement(uint32_t variant) {
+    switch (variant) {
+        case kStepHybridRam: case kStepHybridStackRam: return {true, 0, false};
+        case kStepGlobalAsync: return {false, 1, false};
+        case kStepHybridAsync: return {true, 1, false};
+        case kStepInterleaved: return {true, 0, true};
+        case kStepInterleavedAsync: return {true, 1, true};
+        case kStepGlobalPreload: return {false, 2, false};
+        case kStepHybridPreload: return {true, 2, false};
+        case kStepInterleavedPreload: return {true, 2, true};
+        default: return {false, 0, false};  // kStepGlobalRam
+    }
+}
+
 size_t global_step_smem(uint32_t variant, uint32_t threads) {
-    const bool hybrid = variant == kStepHybridRam || variant == kStepHybridStackRam || variant == kStepHybridAsync;
-    const bool async = variant == kStepGlobalAsync || variant == kStepHybridAsync;
-    return kPrgSmem + kDecSmem + (hybrid ? (size_t)threads * 256 : 0) + (async ? (size_t)threads * kAsyncSmemPerLane : 0);
+    const GlobalPlacement g = global_placement(variant);
+    return kPrgSmem + kDecSmem + (g.hybrid ? (size_t)threads * 256 : 0) +
+           (g.operand == 1 ? (size_t)threads * kAsyncSmemPerLane : 0);
+}
+
+template <uint32_t kVariant>
+cudaError_t configure_global() {
+    constexpr GlobalPlacement g = global_placement(kVariant);
+    return cudaFuncSetAttribute(step_kernel_global<false, g.hybrid, g.operand, g.interleave>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)global_step_smem(kVariant, kGlobalMaxThreads));
+}
+
+template <uint32_t kVariant>
+void launch_global(const BatchView* dv, uint32_t num_envs, const uint8_t* act8, const long long* act64,
+                   uint32_t flags, uint32_t threads, cudaStream_t s) {
+    constexpr GlobalPlacement g = global_placement(kVariant);
+    const uint32_t blocks = (num_envs + threads - 1) / threads;
+    step_kernel_global<false, g.hybrid, g.operand, g.interleave><<<blocks, threads,
+                                                                  global_step_smem(kVariant, threads), s>>>(
+        dv, act8, act64, flags, nullptr, nullptr, kVariant == kStepHybridStackRam ? 0x100u : 0u);
 }
 
 cudaError_t configure_kernels() {
     cudaError_t e = cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)step_smem_bytes());
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(step_kernel_global<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)global_step_smem(kStepHybridRam, kGlobalMaxThreads));
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(step_kernel_global<false, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)global_step_smem(kStepHybridAsync, kGlobalMaxThreads));
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(step_kernel_global<false, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)global_step_smem(kStepGlobalAsync, kGlobalMaxThreads));
+    if (e == cudaSuccess) e = configure_global<kStepGlobalRam>();
+    if (e == cudaSuccess) e = configure_global<kStepHybridRam>();
+    if (e == cudaSuccess) e = configure_global<kStepGlobalAsync>();
+    if (e == cudaSuccess) e = configure_global<kStepHybridAsync>();
+    if (e == cudaSuccess) e = configure_global<kStepInterleaved>();
+    if (e == cudaSuccess) e = configure_global<kStepInterleavedAsync>();
+    if (e == cudaSuccess) e = configure_global<kStepGlobalPreload>();
+    if (e == cudaSuccess) e = configure_global<kStepHybridPreload>();
+    if (e == cudaSuccess) e = configure_global<kStepInterleavedPreload>();
     return e;
 }
 
@@ -722,25 +832,33 @@ cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* a
         const uint32_t blocks = (num_envs + threads - 1) / threads;
         step_kernel_global<true, false><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags, prof_op,
                                                                                     prof_pc, 0);
-    } else if (variant == kStepGlobalRam) {
-        const uint32_t blocks = (num_envs + threads - 1) / threads;
-        step_kernel_global<false, false><<<blocks, threads, global_step_smem(variant, threads), s>>>(
-            dv, act8, act64, flags, nullptr, nullptr, 0);
-    } else if (variant == kStepHybridRam || variant == kStepHybridStackRam) {
-        const uint32_t blocks = (num_envs + threads - 1) / threads;
-        step_kernel_global<false, true><<<blocks, threads, global_step_smem(variant, threads), s>>>(
-            dv, act8, act64, flags, nullptr, nullptr, variant == kStepHybridStackRam ? 0x100u : 0u);
-    } else if (variant == kStepGlobalAsync) {
-        const uint32_t blocks = (num_envs + threads - 1) / threads;
-        step_kernel_global<false, false, true><<<blocks, threads, global_step_smem(variant, threads), s>>>(
-            dv, act8, act64, flags, nullptr, nullptr, 0);
-    } else if (variant == kStepHybridAsync) {
-        const uint32_t blocks = (num_envs + threads - 1) / threads;
-        step_kernel_global<false, true, true><<<blocks, threads, global_step_smem(variant, threads), s>>>(
-            dv, act8, act64, flags, nullptr, nullptr, 0);
     } else {
-        const uint32_t blocks = (num_envs + kStepSlots - 1) / kStepSlots;
-        step_kernel<<<blocks, kStepSlots, step_smem_bytes(), s>>>(dv, act8, act64, flags);
+        switch (variant) {
+            case kStepGlobalRam: launch_global<kStepGlobalRam>(dv, num_envs, act8, act64, flags, threads, s); break;
+            case kStepHybridRam: launch_global<kStepHybridRam>(dv, num_envs, act8, act64, flags, threads, s); break;
+            case kStepHybridStackRam:
+                launch_global<kStepHybridStackRam>(dv, num_envs, act8, act64, flags, threads, s);
+                break;
+            case kStepGlobalAsync: launch_global<kStepGlobalAsync>(dv, num_envs, act8, act64, flags, threads, s); break;
+            case kStepHybridAsync: launch_global<kStepHybridAsync>(dv, num_envs, act8, act64, flags, threads, s); break;
+            case kStepInterleaved: launch_global<kStepInterleaved>(dv, num_envs, act8, act64, flags, threads, s); break;
+            case kStepInterleavedAsync:
+                launch_global<kStepInterleavedAsync>(dv, num_envs, act8, act64, flags, threads, s);
+                break;
+            case kStepGlobalPreload:
+                launch_global<kStepGlobalPreload>(dv, num_envs, act8, act64, flags, threads, s);
+                break;
+            case kStepHybridPreload:
+                launch_global<kStepHybridPreload>(dv, num_envs, act8, act64, flags, threads, s);
+                break;
+            case kStepInterleavedPreload:
+                launch_global<kStepInterleavedPreload>(dv, num_envs, act8, act64, flags, threads, s);
+                break;
+            default: {
+                const uint32_t blocks = (num_envs + kStepSlots - 1) / kStepSlots;
+                step_kernel<<<blocks, kStepSlots, step_smem_bytes(), s>>>(dv, act8, act64, flags);
+            }
+        }
     }
     return cudaGetLastError();
 }

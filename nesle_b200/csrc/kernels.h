@@ -19,7 +19,15 @@ enum : uint32_t {
     kStepHybridStackRam = 3,  // in place, stack page in the slot
     kStepGlobalAsync = 4,     // in place, operands loaded ahead asynchronously
     kStepHybridAsync = 5,     // hybrid, operands outside the slot loaded ahead asynchronously
+    kStepInterleaved = 6,     // hybrid, the rest of RAM in an env-interleaved working copy in device memory
+    kStepInterleavedAsync = 7,  // the same with operands loaded ahead asynchronously
+    kStepGlobalPreload = 8,   // in place, operands loaded one iteration ahead into a register
+    kStepHybridPreload = 9,   // hybrid, the same for operands outside the slot
+    kStepInterleavedPreload = 10,  // interleaved, the same
 };
+inline bool step_interleaved(uint32_t variant) {
+    return variant == kStepInterleaved || variant == kStepInterleavedAsync || variant == kStepInterleavedPreload;
+}
 static_assert(kStepSharedRam == NESLE_PLACEMENT_SHARED && kStepHybridAsync == NESLE_PLACEMENT_HYBRID_ASYNC,
               "step variants are the ABI's placement codes");
 // Dynamic shared memory of one in-place step CTA of `threads` lanes.

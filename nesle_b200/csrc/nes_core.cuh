@@ -880,10 +880,10 @@ NESLE_HD uint32_t effective_address(const Ctx& c, const Lane& L, const Fetched& 
 
 // The instruction at effective address `addr` (page-cross cycle `page`).
 // kAsync: a RAM operand outside the zero-page slot was loaded ahead into
-// `async_word` (the aligned 4-byte word holding it) when `async_ready`.
+// `ahead_byte` when `ahead`.
 template <bool kSharedRam, bool kAsync>
 NESLE_HD uint32_t exec_at(const Ctx& c, Lane& L, Fetched& f, bool& fresh, uint32_t addr, uint32_t page,
-                          bool async_ready, uint32_t async_word) {
+                          bool ahead, uint32_t ahead_byte) {
     const uint32_t pc = L.pc, b1 = f.b1, b2 = f.b2, R = L.R, P = L.p;
     const uint32_t w0 = f.e.w[0], w1 = f.e.w[1], w2 = f.e.w[2], w3 = f.e.w[3], w4 = f.e.w[4], w5 = f.e.w[5];
     const uint32_t wmask = f.e.w[6], spd = f.e.w[7];
@@ -913,7 +913,7 @@ NESLE_HD uint32_t exec_at(const Ctx& c, Lane& L, Fetched& f, bool& fresh, uint32
         mem = *src;
     } else if (kAsync) {
         mem = c.prg[addr & 0x7FFF];
-        if (rd && is_ram) mem = async_ready ? (async_word >> ((addr & 3u) * 8u)) & 0xFFu : (uint32_t)*ram_byte;
+        if (rd && is_ram) mem = ahead ? ahead_byte : (uint32_t)*ram_byte;
     } else {
         mem = c.prg[addr & 0x7FFF];
         if (rd && is_ram) mem = *ram_byte;
@@ -1115,10 +1115,13 @@ NESLE_HD void run_frames(const Ctx& c, Lane& L, const Prof& prof = Prof()) {
 // executes nothing.  Operands in the zero-page slot, PRG ROM, I/O space and
 // immediates are read when the instruction executes, as in run_frames.
 //
-// `Async` provides issue(src) / ready(parity) / word() / drain(); the device
-// implementation uses cp.async with a per-lane mbarrier (kernels.cu), the host
-// build copies at issue time and reports "not ready" on a pseudo-random third
-// of tests to exercise the idle path.
+// `Async` provides issue(byte address) / ready(parity) / byte() / drain().
+// Two device implementations (kernels.cu): cp.async into a shared-memory word
+// with a per-lane mbarrier (lanes idle until their own operand arrives), and a
+// plain load into a register issued one iteration ahead (ready() is always
+// true: the warp waits at the first use, after the independent start of the
+// next iteration).  The host build copies at issue time and reports "not
+// ready" on a pseudo-random quarter of tests to exercise the idle path.
 // ---------------------------------------------------------------------------
 constexpr uint32_t kAsyncSpinLimit = 1u << 22;  // idle iterations one operand may take before the lane stops
 
@@ -1130,7 +1133,7 @@ NESLE_HD bool prepare_operand(const Ctx& c, const Lane& L, const Fetched& f, uin
     addr = effective_address<false>(c, L, f, page);
     const uint32_t w0 = f.e.w[0];
     const bool need = (w0 & E0_RD) && !(w0 & (E0_SPECIAL | E0_ILLEGAL)) && addr < 0x2000u && !in_zp_slot(c, addr);
-    if (need) A.issue(c.ram + (addr & 0x7FCu));
+    if (need) A.issue(c.ram + ram_off(c, addr));
     return need;
 }
 
@@ -1164,9 +1167,9 @@ NESLE_HD void run_frames_async(const Ctx& c, Lane& L, Async& A) {
             }
             continue;
         }
-        uint32_t word = 0;
+        uint32_t ahead = 0;
         if (pend) {
-            word = A.word();
+            ahead = A.byte();
             parity ^= 1u;
             spins = 0;
         }
@@ -1187,7 +1190,7 @@ NESLE_HD void run_frames_async(const Ctx& c, Lane& L, Async& A) {
             fresh = in_prg_window(L.pc) && !L.nmi;
             if (fresh) fetch_prg(c, L.pc, f);
         } else {
-            it_cyc += exec_at<false, true>(c, L, f, fresh, addr, page, pend, word);
+            it_cyc += exec_at<false, true>(c, L, f, fresh, addr, page, pend, ahead);
         }
         pend = false;
         it_cyc += L.dma;
@@ -1208,13 +1211,13 @@ NESLE_HD void run_frames_async(const Ctx& c, Lane& L, Async& A) {
 // Host stand-in for the asynchronous operand load: the copy happens at issue
 // and a deterministic third of the readiness tests say "not yet".
 struct HostAsync {
-    uint32_t w = 0, state = 0x9E3779B9u;
-    NESLE_HD void issue(const uint8_t* src) { memcpy(&w, src, 4); }
+    uint32_t v = 0, state = 0x9E3779B9u;
+    NESLE_HD void issue(const uint8_t* src) { v = *src; }
     NESLE_HD bool ready(uint32_t) {
         state = state * 1664525u + 1013904223u;
         return (state >> 30) != 0u;
     }
-    NESLE_HD uint32_t word() const { return w; }
+    NESLE_HD uint32_t byte() const { return v; }
     NESLE_HD void drain(uint32_t) {}
 };
 

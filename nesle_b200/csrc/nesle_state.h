@@ -147,6 +147,9 @@ typedef struct BatchView {
     uint32_t done_mode, done_a, done_b;
     uint32_t env_offset;
     uint64_t seed;
+    // interleaved placements: the step kernel's working copy of RAM, per CTA
+    // [512 words][lanes][4 bytes] (NULL otherwise)
+    uint8_t* ram_work;
 } BatchView;
 
 #ifdef __cplusplus

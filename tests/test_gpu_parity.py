@@ -19,7 +19,8 @@ from oracle import Oracle
 pytestmark = pytest.mark.gpu
 
 # Every RAM placement of the step kernel (NESLE_STEP_KERNEL).
-PLACEMENTS = ["shared", "global", "hybrid", "hybrid-stack", "global-async", "hybrid-async"]
+PLACEMENTS = ["shared", "global", "hybrid", "hybrid-stack", "global-async", "hybrid-async", "interleaved",
+              "interleaved-async", "global-preload", "hybrid-preload", "interleaved-preload"]
 
 
 @pytest.fixture(scope="module", autouse=True)
