@@ -174,3 +174,37 @@ def _controller_rom() -> bytes:
 
 
 CONTROLLER_ROM = _controller_rom()
+
+
+# The reference VecEnv trace (tests/golden/make_ref_callers.py,
+# tests/test_ref_callers.py): dones that depend on the action, so auto-reset
+# masks are partial.  The NMI handler strobes the controller and reads A; while
+# A is held, $B5 counts up (the SMB predicate's "dying": $B5 > 1), so an env
+# whose action holds A for a whole env-step (4 frames) is done at its end.  It
+# also advances $86 (SMB x) every frame, so rewards are +4 per env-step.  The
+# main loop does indexed RAM work and draws nothing in particular.
+_TRACE_LOOP = 0x8000 + 12  # after the reset code and LDX #0
+ENV_TRACE_ROM = rom_with({
+    0x8000: asm(0x8000, ("LDA", w.IMM, 0x80), ("STA", w.ABS, 0x2000), ("LDA", w.IMM, 0x1E), ("STA", w.ABS, 0x2001),
+                ("LDX", w.IMM, 0x00),
+                ("INC", w.ABS, 0x0300), ("LDA", w.ABS, 0x0300), ("STA", w.ABSX, 0x0400), ("INX",),
+                ("ADC", w.ZP, 0x40), ("STA", w.ZP, 0x40), ("JMP", w.ABS, _TRACE_LOOP)),
+    0x9000: asm(0x9000, ("PHA",), ("LDA", w.IMM, 0x01), ("STA", w.ABS, 0x4016), ("LDA", w.IMM, 0x00),
+                ("STA", w.ABS, 0x4016), ("LDA", w.ABS, 0x4016), ("AND", w.IMM, 0x01), ("BEQ", w.REL, 0x02),
+                ("INC", w.ZP, 0xB5), ("INC", w.ZP, 0x86), ("PLA",), ("RTI",)),
+})
+
+
+def env_trace_snapshots(k: int = 8) -> list[bytes]:
+    """k levels parked at the trace ROM's loop, alive ($0E = 8, $B5 = 0), with
+    different x positions and loop counters, NMI and rendering on."""
+    snaps = []
+    for lvl in range(k):
+        ram = bytearray(2048)
+        ram[0x0E], ram[0xB5], ram[0x75A], ram[0x770] = 8, 0, 2, 1
+        ram[0x86], ram[0x6D] = 16 * lvl, lvl & 1
+        ram[0x300], ram[0x40] = 7 * lvl, lvl
+        ram[0x7F8:0x7FB] = bytes([3, 0, 0])
+        snaps.append(w.write_fcs(w.Snapshot(pc=_TRACE_LOOP, a=lvl, x=3 * lvl, cpu_ram=bytes(ram), ppu_ctrl=0x80,
+                                            ppu_mask=0x1E)))
+    return snaps
