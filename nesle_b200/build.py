@@ -17,7 +17,7 @@ CSRC = PKG / "csrc"
 ROOT = PKG.parent
 LIB = PKG / "libnesle_b200.so"
 SOURCES = ["kernels.cu", "capi.cu", "formats.cpp"]
-DEPS = SOURCES + ["kernels.h", "nes_core.cuh", "nes_render.cuh", "nesle_state.h", "formats.h"]
+DEPS = SOURCES + ["kernels.h", "nes_core.cuh", "nes_render.cuh", "nes_v2.cuh", "nesle_state.h", "formats.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -15,10 +15,18 @@
 #include "kernels.h"
 #include "nes_core.cuh"
 #include "nes_render.cuh"
+#include "nes_v2.cuh"
+
+// NESLE_V2: the shared-RAM and in-place step kernels run the v2 datapath
+// (nes_v2.cuh); the profiled and ahead-loading variants keep the first one.
+#ifndef NESLE_V2
+#define NESLE_V2 1
+#endif
 
 namespace nesle {
 
 __constant__ EntryTable kEntriesConst = dt::build_entries();
+__constant__ EntryTable2 kEntries2Const = dt::build_entries2();
 __constant__ uint8_t kPaletteRgb[192] = NESLE_PALETTE_RGB;
 
 // --------------------------------------------------------------------------
@@ -28,7 +36,16 @@ __constant__ uint8_t kPaletteRgb[192] = NESLE_PALETTE_RGB;
 // (NESLE_STEP_KERNEL=shared forces it); larger batches use the in-place kernel.
 // --------------------------------------------------------------------------
 constexpr uint32_t kPrgSmem = 32768 + 16;  // +16: the two-word fetch at $FFFC-$FFFD reads one word past the ROM
-constexpr uint32_t kDecSmem = 256 * sizeof(Entry);
+constexpr uint32_t kDecSmem = NESLE_V2 ? 256 * sizeof(Entry2) : 256 * sizeof(Entry);  // the table a kernel stages
+
+// Stages the execution entries of the datapath the kernel runs (v2 when
+// kV2) into shared memory at `dst`.
+template <bool kV2>
+__device__ __forceinline__ void stage_entries(uint8_t* dst, uint32_t tid, uint32_t threads) {
+    const uint4* src = kV2 ? reinterpret_cast<const uint4*>(&kEntries2Const) : reinterpret_cast<const uint4*>(&kEntriesConst);
+    const uint32_t n = (kV2 ? sizeof(EntryTable2) : sizeof(EntryTable)) / 16;
+    for (uint32_t i = tid; i < n; i += threads) reinterpret_cast<uint4*>(dst)[i] = src[i];
+}
 
 __device__ __forceinline__ uint32_t* ram_word(uint8_t* slot, uint32_t word) {
     return reinterpret_cast<uint32_t*>(slot + word * 4u * kStepSlots);
@@ -47,8 +64,7 @@ step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
     const uint4* prg_src = reinterpret_cast<const uint4*>(v.prg);
     for (uint32_t i = tid; i < 2048; i += blockDim.x) reinterpret_cast<uint4*>(s_prg)[i] = prg_src[i];
     if (tid == 0) reinterpret_cast<uint4*>(s_prg)[2048] = make_uint4(0, 0, 0, 0);
-    const uint4* ent_src = reinterpret_cast<const uint4*>(&kEntriesConst);
-    for (uint32_t i = tid; i < kDecSmem / 16; i += blockDim.x) reinterpret_cast<uint4*>(s_dec)[i] = ent_src[i];
+    stage_entries<NESLE_V2>(reinterpret_cast<uint8_t*>(s_dec), tid, blockDim.x);
 
     const uint32_t env = blockIdx.x * kStepSlots + tid;
     const bool active = env < v.num_envs;
@@ -76,6 +92,7 @@ step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
     c.zpage = 0;
     c.prg = s_prg;
     c.dec = s_dec;
+    c.dec2 = reinterpret_cast<const Entry2*>(s_dec);
     c.view = vp;
     c.env = env;
     c.frameskip = v.frameskip;
@@ -90,7 +107,8 @@ step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
     const uint8_t action = act64 ? (uint8_t)(act64[env] & 0xFF) : act8[env];
     float reward;
     uint8_t done;
-    run_env_step(c, rec, action, reward, done);
+    if (NESLE_V2) run_env_step_v2<true>(c, rec, action, reward, done);
+    else run_env_step(c, rec, action, reward, done);
 
     uint4* dst = reinterpret_cast<uint4*>(v.ram + (size_t)env * kRamBytes);
 #pragma unroll 4
@@ -214,8 +232,8 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
     const uint4* prg_src = reinterpret_cast<const uint4*>(v.prg);
     for (uint32_t i = tid; i < 2048; i += blockDim.x) reinterpret_cast<uint4*>(s_prg)[i] = prg_src[i];
     if (tid == 0) reinterpret_cast<uint4*>(s_prg)[2048] = make_uint4(0, 0, 0, 0);
-    const uint4* ent_src = reinterpret_cast<const uint4*>(&kEntriesConst);
-    for (uint32_t i = tid; i < kDecSmem / 16; i += blockDim.x) reinterpret_cast<uint4*>(s_dec)[i] = ent_src[i];
+    constexpr bool kV2 = NESLE_V2 && !kProfile && kOperand == 0;  // the datapath this instantiation runs
+    stage_entries<kV2>(reinterpret_cast<uint8_t*>(s_dec), tid, blockDim.x);
     if (kProfile)
         for (uint32_t i = tid; i < 256; i += blockDim.x) s_op[i] = 0;
     __syncthreads();
@@ -258,6 +276,7 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
         }
         c.prg = s_prg;
         c.dec = s_dec;
+        c.dec2 = reinterpret_cast<const Entry2*>(s_dec);
         c.view = vp;
         c.env = env;
         c.frameskip = v.frameskip;
@@ -282,6 +301,8 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
         } else if (kOperand == 2) {
             DevicePreload A;
             run_env_step_async(c, rec, action, reward, done, A);
+        } else if (kV2) {
+            run_env_step_v2<false>(c, rec, action, reward, done);
         } else {
             run_env_step<false>(c, rec, action, reward, done);
         }

@@ -1,0 +1,344 @@
+// nes_v2.cuh -- the 6502 datapath with operand-ready execution entries.
+//
+// Same semantics as exec_uniform / run_frames in nes_core.cuh (cpu.hpp:378-730,
+// kernels.cu:19-104), fewer integer-pipe instructions per emulated
+// instruction.  The step kernel is integer-pipe bound at the occupancy a
+// 65,536-env batch allows (ncu: the ALU pipe busy two thirds of the time, 169
+// ALU-pipe warp instructions per warp iteration); this version spends them on
+// the computation instead of on unpacking table fields:
+//
+//  * a 64-byte execution entry per opcode (Entry2) holds every field as an
+//    operand the datapath uses directly: byte-permute selectors (PRMT) that
+//    pick an index or operand register out of the packed register word,
+//    full-word masks, and multipliers for the operand-B and carry-in terms;
+//  * masks ANDed with values known to be below 256 share their word with other
+//    fields above bit 8 ("dirty" upper bits cost nothing there);
+//  * operand B, the carry-in and the shifter are multiply-adds (the FMA pipe,
+//    which the integer datapath otherwise leaves idle); the shifter yields a
+//    9-bit value with the shifted-out bit at bit 8, like the adder's carry, so
+//    one carry extraction serves both units;
+//  * only the next instruction's three bytes are prefetched (one register);
+//    its entry is loaded at the top of its own iteration, so the prefetch
+//    costs no register moves across the loop's back edge.
+//
+// The header compiles as plain C++ too (the host unit-test build), like
+// nes_core.cuh.
+#pragma once
+#include "nes_core.cuh"
+
+namespace nesle {
+
+// PRMT (byte permute, default mode): result byte n is byte s[4n+2:4n] of the
+// eight bytes {x, y}; if bit 4n+3 of s is set, the sign of that byte is
+// replicated instead.
+NESLE_HD uint32_t prmt(uint32_t x, uint32_t y, uint32_t s) {
+#if defined(__CUDA_ARCH__)
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(x), "r"(y), "r"(s));
+    return d;
+#else
+    const uint64_t v = ((uint64_t)y << 32) | x;
+    uint32_t r = 0;
+    for (uint32_t n = 0; n < 4; ++n) {
+        const uint32_t k = (s >> (4 * n)) & 0xFu;
+        uint32_t b = (uint32_t)(v >> ((k & 7u) * 8u)) & 0xFFu;
+        if (k & 8u) b = (b & 0x80u) ? 0xFFu : 0u;
+        r |= b << (8 * n);
+    }
+    return r;
+#endif
+}
+
+// ---------------------------------------------------------------------------
+// Execution entry v2.
+//   w0  flags (X_*), length at bits 16-17, base cycles at bits 24-27
+//   w1  PRMT selector of the index byte of R (X, Y, SP or zero) | of the
+//       (zp,X) pointer offset (X or zero) << 16
+//   w2  base mask applied to the operand word (0xFF zero page, 0xFFFF absolute)
+//   w3  base increment (1 for stack pulls)
+//   w4  address wrap (0xFF zero page and stack, 0xFFFF otherwise)
+//   w5  address OR (0x100 for the stack)
+//   w6  PRMT selector of operand A over {R, m | (P|$30) << 8}
+//   w7  operand B multiplier (0, 1, -1): B = m * w7 + w8
+//   w8  operand B addend (0, 0xFF; plus 1 where the carry-in is a constant 1)
+//   w9  carry-in multiplier (carry-in = C * w9)
+//   w10 adder result mask (0x1FF: the sum with its carry at bit 8)
+//   w11 AND mask | XOR mask << 8 | shifter mask << 16 (0x1FF, carry at bit 8)
+//   w12 P keep mask | computed mask << 8 | set bits << 16 | from-result mask << 24
+//   w13 branch value (bit 8 set for non-branches: never taken)
+//   w14 branch flag mask (with bit 8) | SP delta byte << 24 (0x01, 0xFF)
+//   w15 register write mask over R = A | X<<8 | Y<<16 | SP<<24
+// ---------------------------------------------------------------------------
+enum : uint32_t {
+    X_ROT = 1u << 0,      // shift rotates through C (bit 0: C & flags & 1 is the rotate-in bit)
+    X_SHL = 1u << 1,
+    X_RD = 1u << 2,
+    X_WM = 1u << 3,
+    X_IMM = 1u << 4,
+    X_JMP = 1u << 5,
+    X_SIDE = 1u << 6,     // JSR RTS RTI BRK JMP(ind) or illegal: the side path
+    X_ILLEGAL = 1u << 7,
+    X_PAGE = 1u << 8,     // bit 8: ANDed with (base ^ addr) it is the page-cross bit
+    X_IND = 1u << 9,
+    X_BIT = 1u << 10,
+};
+
+struct Entry2 {
+    uint32_t w[16];
+};
+struct EntryTable2 {
+    Entry2 e[256];
+};
+
+namespace dt {
+constexpr Entry2 expand2(uint64_t w) {
+    Entry2 e{};
+    const uint32_t idx = F(w, D_IDX, 2), base = F(w, D_BASE, 2), opa = F(w, D_OPA, 3), unit = F(w, D_UNIT, 3);
+    const uint32_t flg = F(w, D_FLG, 2), fcm = F(w, D_FCM, 8);
+    const bool bit = F(w, D_BIT, 1), wp = F(w, D_WP, 1), br = F(w, D_BR, 1), illegal = F(w, D_ILLEGAL, 1);
+    const bool stack = base == 3;
+    uint32_t f = 0;
+    f |= F(w, D_ROT, 1) ? X_ROT : 0u;
+    f |= unit == U_SHL ? X_SHL : 0u;
+    f |= F(w, D_RD, 1) ? X_RD : 0u;
+    f |= F(w, D_WM, 1) ? X_WM : 0u;
+    f |= F(w, D_IMM, 1) ? X_IMM : 0u;
+    f |= F(w, D_JMP, 1) ? X_JMP : 0u;
+    f |= (F(w, D_SPECIAL, 1) || illegal) ? X_SIDE : 0u;
+    f |= illegal ? X_ILLEGAL : 0u;
+    f |= F(w, D_PAGE, 1) ? X_PAGE : 0u;
+    f |= base == 2 ? X_IND : 0u;
+    f |= bit ? X_BIT : 0u;
+    const uint32_t len = illegal ? 1u : F(w, D_LEN, 2) + 1u;
+    e.w[0] = f | (len << 16) | (F(w, D_CYC, 3) << 24);
+    const uint32_t idx_byte = stack ? 3u : idx == 1 ? 1u : idx == 2 ? 2u : 4u;
+    const uint32_t xind_byte = F(w, D_INDX, 1) ? 1u : 4u;
+    e.w[1] = (0x4440u | idx_byte) | ((0x4440u | xind_byte) << 16);
+    e.w[2] = stack || base == 2 ? 0u : base == 0 ? 0xFFu : 0xFFFFu;
+    e.w[3] = stack && F(w, D_PULL, 1) ? 1u : 0u;
+    e.w[4] = (stack || F(w, D_ZPW, 1)) ? 0xFFu : 0xFFFFu;
+    e.w[5] = stack ? 0x100u : 0u;
+    const uint32_t opa_byte = opa == A_A ? 0u : opa == A_X ? 1u : opa == A_Y ? 2u : opa == A_SP ? 3u
+                              : opa == A_M ? 4u : opa == A_PHP ? 5u : 6u;
+    e.w[6] = 0x6660u | opa_byte;
+    const bool bm = F(w, D_BM, 1), bx = F(w, D_BX, 1);
+    e.w[7] = bm ? (bx ? 0xFFFFFFFFu : 1u) : 0u;
+    e.w[8] = (bx ? 0xFFu : 0u) + (F(w, D_CIN1, 1) ? 1u : 0u);
+    e.w[9] = F(w, D_CINC, 1) ? 1u : 0u;
+    e.w[10] = unit == U_ADD ? 0x1FFu : 0u;
+    const bool logic_and = unit == U_AND || unit == U_OR, logic_xor = unit == U_XOR || unit == U_OR;
+    const bool shifter = unit == U_SHL || unit == U_SHR;
+    e.w[11] = (logic_and ? 0xFFu : 0u) | ((logic_xor ? 0xFFu : 0u) << 8) | ((shifter ? 0x1FFu : 0u) << 16);
+    uint32_t comp = flg == F_NZ ? 0x82u : flg == F_NZC ? 0x83u : flg == F_NZCV ? 0xC3u : 0u;
+    if (bit) comp = 0xC2u;
+    uint32_t keep = 0xFFu & ~comp & ~fcm;
+    uint32_t set = F(w, D_FCV, 1) ? fcm : 0u;
+    uint32_t from_r = 0;
+    if (flg || bit || fcm) set |= 0x20u;  // set_flag forces the unused bit (cpu.hpp:52-59)
+    if (wp) { keep = 0; comp = 0; from_r = 0xEFu; set |= 0x20u; }  // PLP: (pulled | $20) & ~$10
+    e.w[12] = keep | (comp << 8) | (set << 16) | (from_r << 24);
+    const uint32_t brmask = br ? (1u << F(w, D_BRF, 3)) : 0u;
+    e.w[13] = br ? (F(w, D_BRP, 1) ? brmask : 0u) : 0x100u;
+    const uint32_t spd = F(w, D_SPD, 2);
+    e.w[14] = (brmask | 0x100u) | ((spd == 1 ? 0xFFu : spd == 2 ? 0x01u : 0u) << 24);
+    e.w[15] = (F(w, D_WA, 1) ? 0xFFu : 0u) | (F(w, D_WX, 1) ? 0xFF00u : 0u) | (F(w, D_WY, 1) ? 0xFF0000u : 0u) |
+              (F(w, D_WSP, 1) ? 0xFF000000u : 0u);
+    return e;
+}
+
+constexpr EntryTable2 build_entries2() {
+    EntryTable2 t{};
+    const DecodeTable d = build();
+    for (int i = 0; i < 256; ++i) t.e[i] = expand2(d.e[i]);
+    return t;
+}
+}  // namespace dt
+
+constexpr EntryTable2 kEntries2Host = dt::build_entries2();
+
+NESLE_HD void load_entry2(const Entry2* table, uint32_t op, Entry2& e) {
+#if defined(__CUDA_ARCH__)
+    const uint4* src = reinterpret_cast<const uint4*>(&table[op]);
+#pragma unroll
+    for (uint32_t q = 0; q < 4; ++q) {
+        const uint4 v = src[q];
+        e.w[4 * q + 0] = v.x;
+        e.w[4 * q + 1] = v.y;
+        e.w[4 * q + 2] = v.z;
+        e.w[4 * q + 3] = v.w;
+    }
+#else
+    e = table[op];
+#endif
+}
+
+// Bytes op | b1 << 8 | b2 << 16 (| junk << 24) at `pc` in the shared PRG copy;
+// memory-safe for any pc, meaningful when in_prg_window(pc).
+NESLE_HD uint32_t fetch_bytes(const Ctx& c, uint32_t pc) {
+    const uint32_t* p32 = reinterpret_cast<const uint32_t*>(c.prg);
+    const uint32_t wi = (pc & 0x7FFFu) >> 2;
+    return NESLE_FUNNEL(p32[wi], p32[wi + 1], pc * 8u);
+}
+
+// The same through the bus, only the bytes the opcode uses, in order
+// (cpu.hpp:382-392, 566-587): code in RAM, PRG-RAM or I/O space.
+NESLE_HD uint32_t fetch_bytes_bus(const Ctx& c, Lane& L) {
+    L.pc &= 0xFFFFu;
+    const uint32_t op = io_rd(c, L, L.pc);
+    const uint32_t len = (c.dec2[op].w[0] >> 16) & 3u;
+    const uint32_t b1 = len >= 2 ? io_rd(c, L, (L.pc + 1) & 0xFFFF) : 0u;
+    const uint32_t b2 = len >= 3 ? io_rd(c, L, (L.pc + 2) & 0xFFFF) : 0u;
+    return op | (b1 << 8) | (b2 << 16);
+}
+
+// One instruction (bytes `nb`, entry `E`) on the uniform datapath; returns its
+// cycles.  On return `nb` holds the next instruction's bytes and `fresh`
+// says whether they are valid (prefetched from the PRG window, no NMI due).
+// The program counter may exceed $FFFF transiently (pc + length, branch
+// targets): such a value is never in the PRG window, so it always goes
+// through the loop top, which masks it.
+template <bool kSharedRam>
+NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, const Entry2& E, bool& fresh) {
+    const uint32_t pc = L.pc, R = L.R, P = L.p, f = E.w[0], bytes = nb;
+    const uint32_t b16 = prmt(bytes, 0u, 0x4421u);
+
+    // ---- next PC (flags from the previous instruction), prefetch ----
+    const uint32_t seq = pc + ((f >> 16) & 3u);
+    const uint32_t target = seq + prmt(bytes, 0u, 0x9991u);  // + sign-extended b1
+    const bool taken = ((P ^ E.w[13]) & E.w[14]) == 0u;  // P ^ w13 < $200: w14's SP byte drops out
+    uint32_t npc = taken ? target : seq;
+    npc = (f & X_JMP) ? b16 : npc;
+    const uint32_t branch_cyc = taken ? 1u + (((seq ^ target) >> 8) & 1u) : 0u;
+    nb = fetch_bytes(c, npc);
+
+    // ---- effective address ----
+    const uint32_t idx = prmt(R, 0u, E.w[1]);
+    uint32_t base = b16 & E.w[2];
+    if (f & X_IND) {
+        const uint32_t zp = (bytes >> 8) + prmt(R, 0u, E.w[1] >> 16);
+        base = ram_rd(c, zp & 0xFFu) | (ram_rd(c, (zp + 1u) & 0xFFu) << 8);
+    }
+    const uint32_t addr = ((base + idx + E.w[3]) & E.w[4]) | E.w[5];
+    const uint32_t page = (((base ^ addr) & f) >> 8) & 1u;  // X_PAGE is bit 8
+    const uint32_t cyc = (f >> 24) + branch_cyc + page;
+
+    // ---- operand ----
+    const bool rd = (f & X_RD) != 0, wm = (f & X_WM) != 0;
+    const bool is_ram = addr < 0x2000u, is_prg = addr >= 0x8000u, is_ctrl = addr == 0x4016u;
+    uint8_t* ram_byte = ram_ptr(c, addr);
+    uint32_t mem;
+    if (kSharedRam) {
+        const uint8_t* src = is_ram ? ram_byte : c.prg + (addr & 0x7FFF);
+        mem = *src;
+    } else {
+        mem = c.prg[addr & 0x7FFF];
+        if (rd && is_ram) mem = *ram_byte;
+    }
+    // $4016: the marker-form shift register (load_lane); while the strobe is
+    // high a read returns the current action's A bit (batch_bus.cuh:110-123).
+    uint32_t m = is_ctrl ? (0x40u | ((L.cstrobe ? L.action : L.csr) & 1u)) : mem;
+    m = (f & X_IMM) ? ((bytes >> 8) & 0xFFu) : m;
+    if (rd && !(is_ram || is_prg || is_ctrl)) m = io_rd(c, L, addr);  // PPU, $4017, PRG-RAM, unmapped
+    const uint32_t shifted = L.csr > 1u ? L.csr >> 1 : L.csr;         // batch_bus.cuh:115-121
+    L.csr = (rd && is_ctrl && !L.cstrobe) ? shifted : L.csr;
+
+    // ---- ALU ----
+    const uint32_t pool = (P | 0x30u) * 256u + m;                 // {m, P|$30, 0, 0}
+    const uint32_t opa = prmt(R, pool, E.w[6]);
+    const uint32_t opb = m * E.w[7] + E.w[8];
+    const uint32_t sum = opa + opb + (P & 1u) * E.w[9];
+    const uint32_t rotc = f & P & 1u;                              // X_ROT is bit 0
+    const uint32_t shl9 = opa * 2u + rotc;                         // result, out bit at 8
+    const uint32_t t9 = rotc * 256u + opa;
+    const uint32_t shr9 = (t9 * 513u) >> 1;                        // (t9 >> 1) | (t9 & 1) << 8
+    const uint32_t sh9 = (f & X_SHL) ? shl9 : shr9;
+    const uint32_t w11 = E.w[11];
+    const uint32_t r9 = (sum & E.w[10]) | (opa & m & w11) | ((opa ^ m) & (w11 >> 8) & 0xFFu) | (sh9 & (w11 >> 16));
+    const uint32_t r = r9 & 0xFFu;
+
+    // ---- flags: P = (P & keep) | (computed & comp) | set | (r & from_r) ----
+    const uint32_t vbit = ((~(opa ^ opb) & (opa ^ r)) >> 1) & 0x40u;
+    const uint32_t nv = (f & X_BIT) ? (m & 0xC0u) : ((r & 0x80u) | vbit);
+    const uint32_t computed = nv | (r == 0u ? 0x02u : 0u) | (r9 >> 8);
+    const uint32_t w12 = E.w[12];
+    const uint32_t p = (P & w12) | (computed & (w12 >> 8) & 0xFFu) | ((w12 >> 16) & 0xFFu) | (r & (w12 >> 24));
+
+    // ---- memory write ----
+    if (wm && is_ram) *ram_byte = (uint8_t)r;
+    const bool cw = wm && is_ctrl;  // $4016 strobe (batch_bus.cuh:125-133)
+    const bool latch = cw && ((r | L.cstrobe) & 1u);
+    L.csr = latch ? L.action : L.csr;
+    L.cstrobe = cw ? (r & 1u) : L.cstrobe;
+    if (wm && !(is_ram || is_prg || is_ctrl)) io_wr(c, L, addr, r);
+
+    // ---- register write-back ----
+    L.R = ((R & ~E.w[15]) | (prmt(r, 0u, 0u) & E.w[15])) + (E.w[14] & 0xFF000000u);
+    L.p = p;
+    L.pc = npc;
+    fresh = in_prg_window(npc) && !L.nmi;
+    return cyc;
+}
+
+// All frames of one env-step on the v2 datapath (run_frames' structure: the
+// loop top, NMI entry and bus fetches on the rare path).
+template <bool kSharedRam>
+NESLE_HD void run_frames_v2(const Ctx& c, Lane& L) {
+    uint32_t nb = 0;
+    bool fresh = false;
+    for (;;) {
+        uint32_t it_cyc = 0;
+        if (!fresh || L.pending >= L.horizon || L.instr >= c.max_instr) {
+            L.pc &= 0xFFFFu;
+            if (!loop_top(c, L)) break;
+            if (L.nmi) {
+                L.nmi = 0;
+                nmi_entry(c, L);
+                it_cyc = 7;
+                fresh = false;
+            }
+            if (!fresh) {
+                nb = in_prg_window(L.pc) ? fetch_bytes(c, L.pc) : fetch_bytes_bus(c, L);
+                fresh = true;
+            }
+        }
+        const uint32_t pc = L.pc, op = nb & 0xFFu;
+        Entry2 E;
+        load_entry2(c.dec2, op, E);
+        if (E.w[0] & X_SIDE) {
+            if (E.w[0] & X_ILLEGAL) {
+                // The reference executes `trap` (cpu.hpp:716-720); the env stops instead.
+                L.status_word = NESLE_STATUS_ILLEGAL | (op << 16) | pc;
+                L.cycles += it_cyc;
+                fresh = false;
+                continue;
+            }
+            exec_special(c, L, op, (nb >> 8) & 0xFFu, (nb >> 16) & 0xFFu);
+            it_cyc += (E.w[0] >> 24) & 0xFu;
+            fresh = in_prg_window(L.pc) && !L.nmi;
+            if (fresh) nb = fetch_bytes(c, L.pc);
+        } else {
+            it_cyc += exec_v2<kSharedRam>(c, L, nb, E, fresh);
+        }
+        it_cyc += L.dma;
+        L.dma = 0;
+        L.cycles += it_cyc;
+        L.pending += it_cyc * 3u;
+        L.instr++;
+        if (op == 0x4C && L.pc == pc) {  // JMP to itself (see run_frames)
+            idle_fast_forward(c, L);
+            fresh = false;
+        }
+    }
+}
+
+template <bool kSharedRam = true>
+NESLE_HD void run_env_step_v2(const Ctx& c, EnvRecord& rec, uint8_t action, float& reward, uint8_t& done) {
+    Lane L;
+    load_lane(L, rec, action);
+    begin_step(L);
+    run_frames_v2<kSharedRam>(c, L);
+    reward_done(c, L, reward, done);
+    store_lane(L, rec);
+}
+
+}  // namespace nesle

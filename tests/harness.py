@@ -59,6 +59,7 @@ class _Common:
 class HostCore(_Common):
     _h_lib = None
     global_ram = False  # subclass HostCoreGlobal runs the in-place RAM variant
+    v2 = True           # the v2 datapath (nes_v2.cuh); the V1 subclasses run the first one
 
     @classmethod
     def lib(cls):
@@ -74,6 +75,7 @@ class HostCore(_Common):
             lib.host_render.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
             lib.host_copy_field.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_uint64]
             lib.host_set_global_ram.argtypes = [ctypes.c_void_p, ctypes.c_int]
+            lib.host_set_v2.argtypes = [ctypes.c_void_p, ctypes.c_int]
             cls._h_lib = lib
         return cls._h_lib
 
@@ -87,6 +89,7 @@ class HostCore(_Common):
             raise ValueError(self.lib().host_last_error().decode())
         self._h = h
         self.lib().host_set_global_ram(h, int(self.global_ram))
+        self.lib().host_set_v2(h, int(self.v2))
 
     def __del__(self):
         if getattr(self, "_h", None):
@@ -131,6 +134,15 @@ class HostCoreHybrid(HostCore):
 
 class HostCoreHybridStack(HostCore):
     global_ram = 3  # in place, stack page in a separate slot
+
+
+class HostCoreV1(HostCore):
+    v2 = False  # RAM in the interleaved slot, first datapath
+
+
+class HostCoreHybridV1(HostCore):
+    global_ram = 2
+    v2 = False
 
 
 class HostCoreGlobalAsync(HostCore):

@@ -15,6 +15,7 @@
 #include "../../nesle_b200/csrc/formats.h"
 #include "../../nesle_b200/csrc/nes_core.cuh"
 #include "../../nesle_b200/csrc/nes_render.cuh"
+#include "../../nesle_b200/csrc/nes_v2.cuh"
 
 using namespace nesle;
 
@@ -34,6 +35,7 @@ struct HostBatch {
     bool global_ram = false;  // run the in-place (global-RAM) variant of the core
     bool hybrid = false;      // ... with one page in a separate slot (hybrid placement)
     bool async = false;       // ... with operands loaded ahead (run_frames_async, HostAsync)
+    bool v2 = true;           // the v2 datapath (nes_v2.cuh), as the product's unprofiled kernels
     uint32_t slot_page = 0;   // the slot's page: 0x000 or 0x100
     std::vector<uint8_t> smem_ram = std::vector<uint8_t>(kSlots * kRamBytes);
 };
@@ -125,6 +127,8 @@ void host_set_global_ram(void* p, int on) {
     h->slot_page = on == 3 ? 0x100u : 0u;
 }
 
+void host_set_v2(void* p, int on) { static_cast<HostBatch*>(p)->v2 = on != 0; }
+
 void host_reset(void* p) {
     auto* h = static_cast<HostBatch*>(p);
     for (uint32_t e = 0; e < h->v.num_envs; ++e) {
@@ -154,6 +158,7 @@ void host_poke_ram(void* p, uint16_t address, uint8_t value) {
 void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) {
     auto* h = static_cast<HostBatch*>(p);
     static const EntryTable& dec_table = kEntriesHost;
+    static const EntryTable2& dec_table2 = kEntries2Host;
     const Entry* dec = dec_table.e;
     for (uint32_t e = 0; e < h->v.num_envs; ++e) {
         const uint32_t slot = e % kSlots;
@@ -163,6 +168,7 @@ void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) 
         c.slots = h->global_ram ? 1 : kSlots;
         c.prg = h->prg.data();
         c.dec = dec;
+        c.dec2 = dec_table2.e;
         c.view = &h->v;
         c.env = e;
         c.frameskip = h->v.frameskip;
@@ -190,12 +196,15 @@ void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) 
                 HostAsync A;
                 A.state ^= e * 0x85EBCA6Bu;  // a different idle pattern per env
                 run_env_step_async(c, rec, actions[e], reward, done, A);
+            } else if (h->v2) {
+                run_env_step_v2<false>(c, rec, actions[e], reward, done);
             } else {
                 run_env_step<false>(c, rec, actions[e], reward, done);
             }
             if (h->hybrid) memcpy(h->ram.data() + (size_t)e * kRamBytes + c.zpage, zp, 256);
         } else {
-            run_env_step<true>(c, rec, actions[e], reward, done);
+            if (h->v2) run_env_step_v2<true>(c, rec, actions[e], reward, done);
+            else run_env_step<true>(c, rec, actions[e], reward, done);
             unstage(*h, e, slot);
         }
         if (finish_env(h->v, e, rec, before, reward, done, device_api != 0, auto_reset != 0)) h->fault++;
