@@ -130,6 +130,7 @@ FIELDS: dict[str, tuple[type, tuple[int, ...]]] = {
     "status": (np.uint32, ()), "stat_instructions": (np.uint64, ()), "stat_frames": (np.uint32, ()),
     "stat_budget_hits": (np.uint32, ()), "frames_rgb": (np.uint8, (240, 256, 3)),
     "frames_index": (np.uint8, (240, 256)), "obs_gray84": (np.uint8, (84, 84)),
+    "prg_bank": (np.uint8, ()), "chr_bank": (np.uint8, ()), "snap_chr_bank": (np.uint8, ()),
 }
 
 _lib = None

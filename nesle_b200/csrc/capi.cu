@@ -71,6 +71,7 @@ struct nesle_batch {
     cudaEvent_t chunk_events[kRenderChunks] = {};  // nesle_render_copy: one per rendered range
     uint32_t step_variant = kStepGlobalRam;
     uint32_t step_threads = 0;
+    bool board = false;  // UxROM / CNROM cartridge
 
     template <class T>
     int alloc(T** out, size_t count, const char* label) {
@@ -222,15 +223,32 @@ static int create_impl(const nesle_create_args* a, nesle_batch* b) {
     CUDA_TRY(cudaMemset(v.last_done, 0, n), "clear last done");
     CUDA_TRY(cudaMemset(v.fault_count, 0, sizeof(uint32_t)), "clear fault count");
 
-    // Cartridge: 16 KB PRG images are mirrored to 32 KB so the kernel masks
-    // every PRG address with $7FFF (cpp/include/nesle/cuda/batch_bus.cuh:24-33).
+    // Cartridge: the 32 KB window at $8000 the kernels stage.  16 KB PRG
+    // images are mirrored to 32 KB so the kernel masks every PRG address with
+    // $7FFF (cpp/include/nesle/cuda/batch_bus.cuh:24-33); for UxROM the window
+    // is bank 0 and the fixed last bank (the kernels serve $8000-$BFFF from
+    // the env's bank of the whole ROM instead).
     std::vector<uint8_t> prg32(32768);
-    for (size_t i = 0; i < 32768; ++i) prg32[i] = cart.prg[i % cart.prg.size()];
+    const size_t last = cart.prg.size() - 16384;
+    for (size_t i = 0; i < 32768; ++i)
+        prg32[i] = cart.mapper == kMapperUxrom ? cart.prg[i < 16384 ? i : last + i - 16384] : cart.prg[i % cart.prg.size()];
     uint8_t* d_prg = nullptr;
     TRY(b->alloc(&d_prg, 32768 + 16, "prg rom"));
     CUDA_TRY(cudaMemset(d_prg, 0, 32768 + 16), "clear prg");
     CUDA_TRY(cudaMemcpy(d_prg, prg32.data(), 32768, cudaMemcpyHostToDevice), "copy prg rom");
     v.prg = d_prg;
+    v.prg_rom = d_prg;
+    if (cart.mapper == kMapperUxrom) {
+        uint8_t* d_rom = nullptr;
+        TRY(b->alloc(&d_rom, cart.prg.size(), "prg banks"));
+        CUDA_TRY(cudaMemcpy(d_rom, cart.prg.data(), cart.prg.size(), cudaMemcpyHostToDevice), "copy prg banks");
+        v.prg_rom = d_rom;
+    }
+    v.mapper = cart.mapper;
+    v.prg_banks = cart.prg_banks;
+    v.chr_banks = cart.chr_banks;
+    TRY(b->alloc(&v.mstate, n, "board registers"));
+    CUDA_TRY(cudaMemset(v.mstate, 0, n * sizeof(MapperState)), "clear board registers");
     v.chr = nullptr;
     v.chr_size = static_cast<uint32_t>(cart.chr.size());
     if (!cart.chr.empty()) {
@@ -324,6 +342,9 @@ static int create_impl(const nesle_create_args* a, nesle_batch* b) {
         else if (strcmp(sv, "hybrid-preload") == 0) b->step_variant = kStepHybridPreload;
         else if (strcmp(sv, "interleaved-preload") == 0) b->step_variant = kStepInterleavedPreload;
     }
+    b->board = cart.mapper != kMapperNrom;
+    if (b->board && b->step_variant != kStepSharedRam && b->step_variant != kStepGlobalRam)
+        b->step_variant = kStepHybridRam;  // the placements built for UxROM / CNROM
     b->step_threads = global_step_threads(b->n, static_cast<uint32_t>(sms));
     if (step_interleaved(b->step_variant)) {  // the interleaved working copy: one 2 KB word column per lane
         const size_t blocks = (b->n + b->step_threads - 1) / b->step_threads;
@@ -407,7 +428,8 @@ static int step_impl(nesle_batch* b, const void* actions, int dtype, int on_devi
         a8 = b->d_host_actions;
     }
     uint32_t flags = (device_api ? kStepDeviceApi : 0u) | (auto_reset ? kStepAutoReset : 0u);
-    return finish(b, s, launch_step(b->dv, b->n, a8, a64, flags, b->step_variant, b->step_threads, s, prof_op, prof_pc),
+    return finish(b, s, launch_step(b->dv, b->n, a8, a64, flags, b->step_variant, b->step_threads, s, prof_op, prof_pc,
+                              b->board),
                   "step kernel");
 }
 
@@ -627,6 +649,18 @@ int nesle_copy_field(nesle_batch* b, const char* name, void* host_out, uint64_t 
             if (!a.ptr) return fail(NESLE_ERR_RUNTIME, "copy_field: " + f + " has not been rendered yet");
             if (bytes != n * a.width) return fail(NESLE_ERR_INVALID, "copy_field: wrong output size for " + f);
             CUDA_TRY(cudaMemcpy(host_out, a.ptr, bytes, cudaMemcpyDeviceToHost), "copy field");
+            return NESLE_OK;
+        }
+    }
+    const char* board_fields[] = {"prg_bank", "chr_bank", "snap_chr_bank"};
+    for (uint32_t k = 0; k < 3; ++k) {
+        if (f == board_fields[k]) {
+            if (bytes != n) return fail(NESLE_ERR_INVALID, "copy_field: wrong output size for " + f);
+            std::vector<MapperState> ms(n);
+            CUDA_TRY(cudaMemcpy(ms.data(), b->hv.mstate, n * sizeof(MapperState), cudaMemcpyDeviceToHost),
+                     "copy board registers");
+            auto* out = static_cast<uint8_t*>(host_out);
+            for (uint64_t e = 0; e < n; ++e) out[e] = reinterpret_cast<const uint8_t*>(&ms[e])[k];
             return NESLE_OK;
         }
     }

@@ -20,9 +20,18 @@ bool parse_ines(const uint8_t* b, size_t len, Cartridge& out, std::string& err) 
     size_t off = 16 + ((f6 & 0x04) ? 512 : 0);
     const size_t prg = static_cast<size_t>(prg_banks) * 16384, chr = static_cast<size_t>(chr_banks) * 8192;
     if (len < off + prg + chr) { err = "iNES data is truncated for declared PRG/CHR sizes"; return false; }
-    // cuda_module.cu:381-398 (console path: NROM only, PRG 16/32 KB)
-    if (mapper != 0 || (prg_banks != 1 && prg_banks != 2)) {
-        err = "CUDA console mode currently supports mapper 0/NROM ROMs";
+    // cuda_module.cu:381-398 accepts NROM only (mapper 0, PRG 16/32 KB).  This
+    // core also runs the two discrete-logic boards (no counterpart in the
+    // reference): UxROM (mapper 2: 2-16 PRG banks of 16 KB, a power of two,
+    // switchable at $8000, the last one fixed at $C000) and CNROM (mapper 3:
+    // 16/32 KB PRG, 1-4 CHR banks of 8 KB, a power of two).
+    const auto pow2 = [](unsigned n) { return n != 0 && (n & (n - 1)) == 0; };
+    const bool nrom = mapper == 0 && (prg_banks == 1 || prg_banks == 2);
+    const bool uxrom = mapper == 2 && prg_banks >= 2 && prg_banks <= 16 && pow2(prg_banks) && chr_banks <= 1;
+    const bool cnrom = mapper == 3 && (prg_banks == 1 || prg_banks == 2) && chr_banks <= 4 && pow2(chr_banks);
+    if (!nrom && !uxrom && !cnrom) {
+        err = "supported cartridges: mapper 0/NROM (16/32 KB PRG), 2/UxROM (32-256 KB PRG, power-of-two banks, "
+              "8 KB CHR) and 3/CNROM (16/32 KB PRG, 8-32 KB CHR, power-of-two banks)";
         return false;
     }
     if (f6 & 0x08) {

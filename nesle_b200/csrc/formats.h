@@ -9,7 +9,7 @@
 namespace nesle {
 
 struct Cartridge {
-    std::vector<uint8_t> prg;  // 16 or 32 KB as stored in the image
+    std::vector<uint8_t> prg;  // 16 or 32 KB (NROM, CNROM) or 32-256 KB (UxROM) as stored in the image
     std::vector<uint8_t> chr;  // 0 or N * 8 KB
     uint16_t mapper = 0;
     uint8_t prg_banks = 0, chr_banks = 0;
@@ -18,8 +18,8 @@ struct Cartridge {
 };
 
 // Parses an iNES/NES 2.0 image and applies the reference binding's checks for
-// the console path (cpp/src/rom.cpp:65-121, cpp/bindings/cuda_module.cu:381-398).
-// Returns false with `err` set on failure.
+// the console path (cpp/src/rom.cpp:65-121, cpp/bindings/cuda_module.cu:381-398),
+// widened to the UxROM and CNROM boards.  Returns false with `err` set on failure.
 bool parse_ines(const uint8_t* data, size_t len, Cartridge& out, std::string& err);
 
 // One FCS save state (cpp/include/nesle/fcs.hpp:19-45).

@@ -51,6 +51,10 @@ __device__ __forceinline__ uint32_t* ram_word(uint8_t* slot, uint32_t word) {
     return reinterpret_cast<uint32_t*>(slot + word * 4u * kStepSlots);
 }
 
+// kBoard: the cartridge may be UxROM or CNROM (Ctx::prg_lo / prg_writes at
+// run time); NROM batches run the kBoard = false instantiations, where both
+// are constants.
+template <bool kBoard>
 __global__ void __launch_bounds__(kStepSlots, 1)
 step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
             const long long* __restrict__ act64, uint32_t flags) {
@@ -101,6 +105,8 @@ step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
     c.nt = v.nt + (size_t)env * kNtBytes;
     c.pal = v.pal + (size_t)env * kPalBytes;
     c.oam = v.oam + (size_t)env * kOamBytes;
+    c.prg_lo = kBoard && v.mapper == kMapperUxrom ? 0xC000u : 0x8000u;
+    c.prg_writes = kBoard;
 
     EnvRecord rec = v.rec[env];
     const uint32_t status_before = rec.status;
@@ -216,7 +222,7 @@ struct DevicePreload {
 // l at (w * lanes + l) * 4), so the same address of the 32 envs of a warp is
 // one 128-byte line instead of 32 rows; copied in at the start and back at the
 // end of the launch.
-template <bool kProfile, bool kHybrid, int kOperand = 0, bool kInterleave = false>
+template <bool kProfile, bool kHybrid, int kOperand = 0, bool kInterleave = false, bool kBoard = false>
 __global__ void __launch_bounds__(kGlobalMaxThreads, 1)
 step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
                    const long long* __restrict__ act64, uint32_t flags, unsigned long long* __restrict__ prof_op,
@@ -285,6 +291,8 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
         c.nt = v.nt + (size_t)env * kNtBytes;
         c.pal = v.pal + (size_t)env * kPalBytes;
         c.oam = v.oam + (size_t)env * kOamBytes;
+        c.prg_lo = kBoard && v.mapper == kMapperUxrom ? 0xC000u : 0x8000u;
+        c.prg_writes = kBoard;
 
         EnvRecord rec = v.rec[env];
         const uint32_t status_before = rec.status;
@@ -366,16 +374,19 @@ state_kernel(const BatchView* __restrict__ vp, const uint32_t* __restrict__ envs
     if (threadIdx.x == 0) {
         float* f = reinterpret_cast<float*>(blob + kStateOut);
         uint8_t* u = blob + kStateOut + 8;
+        MapperState* ms = reinterpret_cast<MapperState*>(blob + kStateOut + 12);
         if (s) {
             f[0] = v.rewards[env];
             f[1] = v.last_rewards[env];
             u[0] = v.done[env];
             u[1] = v.last_done[env];
+            *ms = v.mstate[env];
         } else {
             v.rewards[env] = f[0];
             v.last_rewards[env] = f[1];
             v.done[env] = u[0];
             v.last_done[env] = u[1];
+            v.mstate[env] = *ms;
         }
     }
 }
@@ -397,7 +408,10 @@ reset_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ mask,
         if (full) rec.episode = 0;
         else rec.episode++;
         reset_record(v, env, rec);
-        if (full) seed_presentation_record(rec);
+        if (full) {
+            seed_presentation_record(rec);
+            seed_presentation_board(v, env);
+        }
         v.rec[env] = rec;
         v.rewards[env] = 0.0f;
         v.done[env] = 0;
@@ -437,9 +451,11 @@ struct SnapSmem {
 
 __device__ __forceinline__ RenderEnv stage_snapshot(const BatchView& v, uint32_t env, SnapSmem& sm) {
     const uint32_t tid = threadIdx.x;
-    const uint32_t chr_size = v.chr_size <= kChrMax ? v.chr_size : 0u;
+    uint32_t chr_size;
+    const uint8_t* chr = snapshot_chr(v, env, chr_size);  // CNROM: the bank latched at vblank
+    if (chr_size > kChrMax) chr_size = 0u;
     for (uint32_t i = tid; i < chr_size / 16; i += blockDim.x)
-        reinterpret_cast<uint4*>(sm.chr)[i] = reinterpret_cast<const uint4*>(v.chr)[i];
+        reinterpret_cast<uint4*>(sm.chr)[i] = reinterpret_cast<const uint4*>(chr)[i];
     const uint4* nt = reinterpret_cast<const uint4*>(v.snap_nt + (size_t)env * kNtBytes);
     for (uint32_t i = tid; i < kNtBytes / 16; i += blockDim.x) reinterpret_cast<uint4*>(sm.nt)[i] = nt[i];
     if (tid < kOamBytes / 16)
@@ -802,26 +818,31 @@ size_t global_step_smem(uint32_t variant, uint32_t threads) {
            (g.operand == 1 ? (size_t)threads * kAsyncSmemPerLane : 0);
 }
 
-template <uint32_t kVariant>
+template <uint32_t kVariant, bool kBoard = false>
 cudaError_t configure_global() {
     constexpr GlobalPlacement g = global_placement(kVariant);
-    return cudaFuncSetAttribute(step_kernel_global<false, g.hybrid, g.operand, g.interleave>,
+    return cudaFuncSetAttribute(step_kernel_global<false, g.hybrid, g.operand, g.interleave, kBoard>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)global_step_smem(kVariant, kGlobalMaxThreads));
 }
 
-template <uint32_t kVariant>
+template <uint32_t kVariant, bool kBoard = false>
 void launch_global(const BatchView* dv, uint32_t num_envs, const uint8_t* act8, const long long* act64,
                    uint32_t flags, uint32_t threads, cudaStream_t s) {
     constexpr GlobalPlacement g = global_placement(kVariant);
     const uint32_t blocks = (num_envs + threads - 1) / threads;
-    step_kernel_global<false, g.hybrid, g.operand, g.interleave><<<blocks, threads,
-                                                                  global_step_smem(kVariant, threads), s>>>(
+    step_kernel_global<false, g.hybrid, g.operand, g.interleave, kBoard><<<blocks, threads,
+                                                                          global_step_smem(kVariant, threads), s>>>(
         dv, act8, act64, flags, nullptr, nullptr, kVariant == kStepHybridStackRam ? 0x100u : 0u);
 }
 
 cudaError_t configure_kernels() {
-    cudaError_t e = cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)step_smem_bytes());
+    cudaError_t e = cudaFuncSetAttribute(step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)step_smem_bytes());
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)step_smem_bytes());
+    if (e == cudaSuccess) e = configure_global<kStepGlobalRam, true>();
+    if (e == cudaSuccess) e = configure_global<kStepHybridRam, true>();
     if (e == cudaSuccess) e = configure_global<kStepGlobalRam>();
     if (e == cudaSuccess) e = configure_global<kStepHybridRam>();
     if (e == cudaSuccess) e = configure_global<kStepGlobalAsync>();
@@ -847,12 +868,25 @@ uint32_t global_step_threads(uint32_t num_envs, uint32_t num_sms) {
 
 cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* act8, const long long* act64,
                         uint32_t flags, uint32_t variant, uint32_t threads, cudaStream_t s,
-                        unsigned long long* prof_op, unsigned long long* prof_pc) {
+                        unsigned long long* prof_op, unsigned long long* prof_pc, bool board) {
     if (prof_op || prof_pc) {  // step_profile: the in-place kernel with histograms
         if (!prof_op || !prof_pc) return cudaErrorInvalidValue;
         const uint32_t blocks = (num_envs + threads - 1) / threads;
-        step_kernel_global<true, false><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags, prof_op,
-                                                                                    prof_pc, 0);
+        if (board)
+            step_kernel_global<true, false, 0, false, true><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(
+                dv, act8, act64, flags, prof_op, prof_pc, 0);
+        else
+            step_kernel_global<true, false><<<blocks, threads, kPrgSmem + kDecSmem, s>>>(dv, act8, act64, flags,
+                                                                                        prof_op, prof_pc, 0);
+    } else if (board) {  // UxROM / CNROM: the shared, in-place and hybrid placements
+        if (variant == kStepGlobalRam) {
+            launch_global<kStepGlobalRam, true>(dv, num_envs, act8, act64, flags, threads, s);
+        } else if (variant == kStepHybridRam) {
+            launch_global<kStepHybridRam, true>(dv, num_envs, act8, act64, flags, threads, s);
+        } else {
+            const uint32_t blocks = (num_envs + kStepSlots - 1) / kStepSlots;
+            step_kernel<true><<<blocks, kStepSlots, step_smem_bytes(), s>>>(dv, act8, act64, flags);
+        }
     } else {
         switch (variant) {
             case kStepGlobalRam: launch_global<kStepGlobalRam>(dv, num_envs, act8, act64, flags, threads, s); break;
@@ -877,7 +911,7 @@ cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* a
                 break;
             default: {
                 const uint32_t blocks = (num_envs + kStepSlots - 1) / kStepSlots;
-                step_kernel<<<blocks, kStepSlots, step_smem_bytes(), s>>>(dv, act8, act64, flags);
+                step_kernel<false><<<blocks, kStepSlots, step_smem_bytes(), s>>>(dv, act8, act64, flags);
             }
         }
     }

@@ -39,9 +39,11 @@ size_t step_smem_bytes();
 cudaError_t configure_kernels();
 uint32_t global_step_threads(uint32_t num_envs, uint32_t num_sms);
 // prof_op (256) / prof_pc (65536): step_profile histograms to add to, or both null.
+// board: the cartridge is UxROM or CNROM (variant must then be shared, global or hybrid).
 cudaError_t launch_step(const BatchView* dv, uint32_t num_envs, const uint8_t* act8, const long long* act64,
                         uint32_t flags, uint32_t variant, uint32_t threads, cudaStream_t s,
-                        unsigned long long* prof_op = nullptr, unsigned long long* prof_pc = nullptr);
+                        unsigned long long* prof_op = nullptr, unsigned long long* prof_pc = nullptr,
+                        bool board = false);
 cudaError_t launch_reset(const BatchView* dv, uint32_t num_envs, const uint8_t* mask, bool full, cudaStream_t s);
 // envs: device array of `count` env indices; blobs: count x kStateBytes (device).
 cudaError_t launch_state(const BatchView* dv, const uint32_t* envs, uint32_t count, uint8_t* blobs, bool save,

@@ -475,6 +475,12 @@ struct Ctx {
     uint8_t* nt;
     uint8_t* pal;
     uint8_t* oam;
+    // Cartridge board: the PRG addresses the shared 32 KB copy serves
+    // ([prg_lo, $FFFF]: $8000 for NROM and CNROM, $C000 for UxROM, whose
+    // $8000-$BFFF bank is per env) and whether writes to $8000-$FFFF reach the
+    // bus (board registers).  NROM kernels set both as constants.
+    uint32_t prg_lo;
+    bool prg_writes;
 };
 
 NESLE_HD uint32_t ram_off(const Ctx& c, uint32_t a) { return (a & 0x7FCu) * c.slots + (a & 3u); }
@@ -523,9 +529,38 @@ NESLE_HD uint32_t mirror_nt(uint32_t horizontal, uint32_t a) {
     uint32_t i = (a - 0x2000u) & 0x0FFFu;
     return horizontal ? ((i & 0x03FFu) | ((i & 0x0800u) >> 1)) : (i & 0x07FFu);
 }
+// The env's board registers (UxROM, CNROM).
+NESLE_HD MapperState& mapper_state(const Ctx& c) { return c.view->mstate[c.env]; }
+
+// CHR byte `a` ($0000-$1FFF) through the board: CNROM selects an 8 KB bank.
+NESLE_HD uint32_t chr_rd(const Ctx& c, uint32_t a) {
+    const BatchView& v = *c.view;
+    if (!v.chr_size) return 0u;
+    const uint32_t off = v.mapper == kMapperCnrom ? (uint32_t)mapper_state(c).chr_bank * 8192u : 0u;
+    return v.chr[(off + a) % v.chr_size];
+}
+
+// PRG byte `a` ($8000-$FFFF) through the board: UxROM's $8000-$BFFF is the
+// env's bank of the whole PRG ROM; everything else is in the 32 KB copy.
+NESLE_HD uint32_t prg_rd(const Ctx& c, uint32_t a) {
+    if (a < c.prg_lo) return c.view->prg_rom[(uint32_t)mapper_state(c).prg_bank * 0x4000u + (a & 0x3FFFu)];
+    return c.prg[a & 0x7FFF];
+}
+
+// Write to the board register at $8000-$FFFF (bus conflict: the ROM drives the
+// data bus too, so the value is ANDed with the PRG byte at that address).
+NESLE_HD void board_wr(const Ctx& c, uint32_t a, uint32_t val) {
+    const BatchView& v = *c.view;
+    if (v.mapper == kMapperNrom) return;
+    val &= prg_rd(c, a);
+    MapperState& ms = mapper_state(c);
+    if (v.mapper == kMapperUxrom) ms.prg_bank = (uint8_t)(val & (v.prg_banks - 1u));
+    else ms.chr_bank = (uint8_t)(val & (v.chr_banks - 1u));
+}
+
 NESLE_HD uint32_t ppu_mem_rd(const Ctx& c, uint32_t a) {
     a &= 0x3FFF;
-    if (a < 0x2000) return c.view->chr_size ? c.view->chr[a % c.view->chr_size] : 0u;
+    if (a < 0x2000) return chr_rd(c, a);
     if (a < 0x3F00) {
         if (a >= 0x3000) a -= 0x1000;
         return c.nt[mirror_nt(c.view->horizontal, a)];
@@ -606,7 +641,7 @@ NESLE_HD uint32_t io_rd(const Ctx& c, Lane& L, uint32_t a) {
     }
     if (a == 0x4017) return 0x41;
     if (a >= 0x6000 && a < 0x8000) return c.prg_ram[a - 0x6000];
-    if (a >= 0x8000) return c.prg[a & 0x7FFF];
+    if (a >= 0x8000) return prg_rd(c, a);
     return 0;
 }
 
@@ -664,6 +699,7 @@ NESLE_HD void io_wr(const Ctx& c, Lane& L, uint32_t a, uint32_t val) {
         return;
     }
     if (a >= 0x6000 && a < 0x8000) c.prg_ram[a - 0x6000] = (uint8_t)val;
+    if (a >= 0x8000) board_wr(c, a, val);
 }
 
 // Fast-path predicates: RAM and PRG reads have no side effects; writes to
@@ -729,6 +765,10 @@ NESLE_HD void presentation_snapshot(const Ctx& c, Lane& L) {
     if (L.flags & kFlagNtDirty) copy_row(v.snap_nt + e * kNtBytes, c.nt, kNtBytes);
     if (L.flags & kFlagPalDirty) copy_row(v.snap_pal + e * kPalBytes, c.pal, kPalBytes);
     L.flags &= ~(uint32_t)(kFlagOamDirty | kFlagNtDirty | kFlagPalDirty);
+    if (v.mapper == kMapperCnrom) {
+        MapperState& ms = mapper_state(c);
+        ms.snap_chr_bank = ms.chr_bank;
+    }
 }
 
 // batch_ppu.cuh:183-269; returns frames completed.
@@ -818,7 +858,9 @@ struct Fetched {
     Entry e;
 };
 
-NESLE_HD bool in_prg_window(uint32_t pc) { return pc - 0x8000u <= 0x7FFDu; }
+// pc is in the shared PRG copy with two bytes after it ($FFFE-$FFFF start
+// instructions through the bus).
+NESLE_HD bool in_prg_window(const Ctx& c, uint32_t pc) { return pc - c.prg_lo <= 0xFFFDu - c.prg_lo; }
 
 NESLE_HD void load_entry(const Ctx& c, uint32_t op, Entry& e) {
 #if defined(__CUDA_ARCH__)
@@ -908,7 +950,8 @@ NESLE_HD uint32_t exec_at(const Ctx& c, Lane& L, Fetched& f, bool& fresh, uint32
     // ---- operand read: RAM/PRG from fast memory, $4016/$4017 and the
     //      unmapped $4000-$5FFF reads inline, PPU registers and PRG-RAM aside ----
     const bool rd = (w0 & E0_RD) != 0, wm = (w0 & E0_WM) != 0;
-    const bool is_ram = addr < 0x2000u, is_prg = addr >= 0x8000u, is_ctrl = addr == 0x4016u;
+    const bool is_ram = addr < 0x2000u, is_prg = addr >= c.prg_lo, is_ctrl = addr == 0x4016u;
+    const bool banked = addr >= 0x8000u && !is_prg;  // UxROM's switchable bank: through the bus
     // Hybrid placement: ram_ptr points into the zero-page slot or the row, and
     // the operand is one (generic) access either way.
     uint8_t* ram_byte = ram_ptr(c, addr);
@@ -927,7 +970,7 @@ NESLE_HD uint32_t exec_at(const Ctx& c, Lane& L, Fetched& f, bool& fresh, uint32
     uint32_t m = (is_ram || is_prg) ? mem : (is_ctrl ? (0x40u | cbit) : (addr == 0x4017u ? 0x41u : 0u));
     m = (w0 & E0_IMM) ? b1 : m;
     const bool io_space = (addr - 0x2000u < 0x2000u) || (addr - 0x6000u < 0x2000u);
-    if (rd && io_space) m = io_rd(c, L, addr);
+    if (rd && (io_space || banked)) m = io_rd(c, L, addr);
     const bool shift_now = rd && is_ctrl && !L.cstrobe && L.csr > 1u;  // batch_bus.cuh:115-121
     L.csr = shift_now ? (L.csr >> 1) : L.csr;
 
@@ -958,7 +1001,7 @@ NESLE_HD uint32_t exec_at(const Ctx& c, Lane& L, Fetched& f, bool& fresh, uint32
     const bool latch = cw && ((r & 1u) || L.cstrobe);
     L.csr = latch ? L.action : L.csr;
     L.cstrobe = cw ? (r & 1u) : L.cstrobe;
-    if (wm && (io_space || addr == 0x4014u)) io_wr(c, L, addr, r);
+    if (wm && (io_space || addr == 0x4014u || (c.prg_writes && addr >= 0x8000u))) io_wr(c, L, addr, r);
 
     // ---- register write-back ----
     L.R = ((R & ~wmask) | ((r * 0x01010101u) & wmask)) + spd;
@@ -967,7 +1010,7 @@ NESLE_HD uint32_t exec_at(const Ctx& c, Lane& L, Fetched& f, bool& fresh, uint32
     f = nf;
     // The prefetch stays valid after I/O side effects (PRG ROM cannot change);
     // only a pending NMI, which a $2000 write can raise, needs the loop top.
-    fresh = in_prg_window(npc) && !L.nmi;
+    fresh = in_prg_window(c, npc) && !L.nmi;
     return cyc;
 }
 
@@ -1064,7 +1107,7 @@ NESLE_HD void run_frames(const Ctx& c, Lane& L, const Prof& prof = Prof()) {
                 fresh = false;
             }
             if (!fresh) {
-                if (in_prg_window(L.pc)) fetch_prg(c, L.pc, f);
+                if (in_prg_window(c, L.pc)) fetch_prg(c, L.pc, f);
                 else fetch_bus(c, L, f);
                 fresh = true;
             }
@@ -1080,7 +1123,7 @@ NESLE_HD void run_frames(const Ctx& c, Lane& L, const Prof& prof = Prof()) {
             }
             exec_special(c, L, op, f.b1, f.b2);
             it_cyc += byte_of(f.e.w[0], 3);
-            fresh = in_prg_window(L.pc) && !L.nmi;
+            fresh = in_prg_window(c, L.pc) && !L.nmi;
             if (fresh) fetch_prg(c, L.pc, f);
         } else {
             it_cyc += exec_uniform<kSharedRam>(c, L, f, fresh);
@@ -1159,7 +1202,7 @@ NESLE_HD void run_frames_async(const Ctx& c, Lane& L, Async& A) {
                 fresh = false;
             }
             if (!fresh) {
-                if (in_prg_window(L.pc)) fetch_prg(c, L.pc, f);
+                if (in_prg_window(c, L.pc)) fetch_prg(c, L.pc, f);
                 else fetch_bus(c, L, f);
                 fresh = true;
             }
@@ -1192,7 +1235,7 @@ NESLE_HD void run_frames_async(const Ctx& c, Lane& L, Async& A) {
             }
             exec_special(c, L, op, f.b1, f.b2);
             it_cyc += byte_of(f.e.w[0], 3);
-            fresh = in_prg_window(L.pc) && !L.nmi;
+            fresh = in_prg_window(c, L.pc) && !L.nmi;
             if (fresh) fetch_prg(c, L.pc, f);
         } else {
             it_cyc += exec_at<false, true>(c, L, f, fresh, addr, page, pend, ahead);
@@ -1321,6 +1364,10 @@ NESLE_HD void reset_rows(const BatchView& v, uint32_t env, uint32_t lane, uint32
 // presentation-snapshot scalars and the per-step statistics of the step that
 // triggered the reset survive.
 NESLE_HD void reset_record(const BatchView& v, uint32_t env, EnvRecord& r) {
+    if (v.mstate) {  // board registers reset to bank 0; the CHR bank of the presentation snapshot survives
+        v.mstate[env].prg_bank = 0;
+        v.mstate[env].chr_bank = 0;
+    }
     const EnvRecord keep = r;
     if (v.num_levels) warm_reset_record(v, env, r);
     else cold_reset_record(v, r);
@@ -1354,9 +1401,13 @@ NESLE_HD void seed_presentation_rows(const BatchView& v, uint32_t env, uint32_t 
     copy_part(v.snap_pal + e * kPalBytes, v.pal + e * kPalBytes, kPalBytes, lane, lanes);
     copy_part(v.snap_oam + e * kOamBytes, v.oam + e * kOamBytes, kOamBytes, lane, lanes);
 }
+NESLE_HD void seed_presentation_board(const BatchView& v, uint32_t env) {
+    if (v.mstate) v.mstate[env].snap_chr_bank = v.mstate[env].chr_bank;
+}
 NESLE_HD void seed_presentation(const BatchView& v, uint32_t env, EnvRecord& r) {
     seed_presentation_rows(v, env, 0, 1);
     seed_presentation_record(r);
+    seed_presentation_board(v, env);
 }
 
 // ---------------------------------------------------------------------------

@@ -135,9 +135,22 @@ NESLE_HD RenderEnv render_env_at(const EnvRecord& r, const uint8_t* nt, const ui
     return e;
 }
 
+// The pattern tables a presentation snapshot renders with: the whole CHR
+// ROM, or for CNROM the 8 KB bank latched at vblank.
+NESLE_HD const uint8_t* snapshot_chr(const BatchView& bv, uint32_t env, uint32_t& size) {
+    if (bv.mapper == kMapperCnrom && bv.chr_size) {
+        size = 8192u;
+        return bv.chr + (size_t)bv.mstate[env].snap_chr_bank * 8192u;
+    }
+    size = bv.chr_size;
+    return bv.chr;
+}
+
 NESLE_HD RenderEnv render_env(const BatchView& bv, const EnvRecord& r, uint32_t env) {
+    uint32_t chr_size;
+    const uint8_t* chr = snapshot_chr(bv, env, chr_size);
     return render_env_at(r, bv.snap_nt + (size_t)env * kNtBytes, bv.snap_pal + (size_t)env * kPalBytes,
-                         bv.snap_oam + (size_t)env * kOamBytes, bv.chr, bv.chr_size, bv.horizontal);
+                         bv.snap_oam + (size_t)env * kOamBytes, chr, chr_size, bv.horizontal);
 }
 
 // Bit i set when sprite i covers scanline y (the row test of the sprite loop,

@@ -224,7 +224,7 @@ NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, const Entry2& E, 
 
     // ---- operand ----
     const bool rd = (f & X_RD) != 0, wm = (f & X_WM) != 0;
-    const bool is_ram = addr < 0x2000u, is_prg = addr >= 0x8000u, is_ctrl = addr == 0x4016u;
+    const bool is_ram = addr < 0x2000u, is_prg = addr >= c.prg_lo, is_ctrl = addr == 0x4016u;
     uint8_t* ram_byte = ram_ptr(c, addr);
     uint32_t mem;
     if (kSharedRam) {
@@ -238,7 +238,7 @@ NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, const Entry2& E, 
     // high a read returns the current action's A bit (batch_bus.cuh:110-123).
     uint32_t m = is_ctrl ? (0x40u | ((L.cstrobe ? L.action : L.csr) & 1u)) : mem;
     m = (f & X_IMM) ? ((bytes >> 8) & 0xFFu) : m;
-    if (rd && !(is_ram || is_prg || is_ctrl)) m = io_rd(c, L, addr);  // PPU, $4017, PRG-RAM, unmapped
+    if (rd && !(is_ram || is_prg || is_ctrl)) m = io_rd(c, L, addr);  // PPU, $4017, PRG-RAM, banked PRG, unmapped
     const uint32_t shifted = L.csr > 1u ? L.csr >> 1 : L.csr;         // batch_bus.cuh:115-121
     L.csr = (rd && is_ctrl && !L.cstrobe) ? shifted : L.csr;
 
@@ -269,13 +269,13 @@ NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, const Entry2& E, 
     const bool latch = cw && ((r | L.cstrobe) & 1u);
     L.csr = latch ? L.action : L.csr;
     L.cstrobe = cw ? (r & 1u) : L.cstrobe;
-    if (wm && !(is_ram || is_prg || is_ctrl)) io_wr(c, L, addr, r);
+    if (wm && !(is_ram || (is_prg && !c.prg_writes) || is_ctrl)) io_wr(c, L, addr, r);
 
     // ---- register write-back ----
     L.R = ((R & ~E.w[15]) | (prmt(r, 0u, 0u) & E.w[15])) + (E.w[14] & 0xFF000000u);
     L.p = p;
     L.pc = npc;
-    fresh = in_prg_window(npc) && !L.nmi;
+    fresh = in_prg_window(c, npc) && !L.nmi;
     return cyc;
 }
 
@@ -297,7 +297,7 @@ NESLE_HD void run_frames_v2(const Ctx& c, Lane& L) {
                 fresh = false;
             }
             if (!fresh) {
-                nb = in_prg_window(L.pc) ? fetch_bytes(c, L.pc) : fetch_bytes_bus(c, L);
+                nb = in_prg_window(c, L.pc) ? fetch_bytes(c, L.pc) : fetch_bytes_bus(c, L);
                 fresh = true;
             }
         }
@@ -314,7 +314,7 @@ NESLE_HD void run_frames_v2(const Ctx& c, Lane& L) {
             }
             exec_special(c, L, op, (nb >> 8) & 0xFFu, (nb >> 16) & 0xFFu);
             it_cyc += (E.w[0] >> 24) & 0xFu;
-            fresh = in_prg_window(L.pc) && !L.nmi;
+            fresh = in_prg_window(c, L.pc) && !L.nmi;
             if (fresh) nb = fetch_bytes(c, L.pc);
         } else {
             it_cyc += exec_v2<kSharedRam>(c, L, nb, E, fresh);

@@ -96,9 +96,26 @@ enum {
     kStateSnapNt = kStateOam + kOamBytes,        // 2048
     kStateSnapPal = kStateSnapNt + kNtBytes,     // 32
     kStateSnapOam = kStateSnapPal + kPalBytes,   // 256
-    kStateOut = kStateSnapOam + kOamBytes,       // reward f32, last reward f32, done u8, last done u8, pad
+    kStateOut = kStateSnapOam + kOamBytes,       // reward f32, last reward f32, done u8, last done u8,
+                                                 // MapperState (4 bytes at +12)
     kStateBytes = kStateOut + 16,                // 15,056
 };
+
+// Cartridge boards (iNES mapper numbers).
+enum {
+    kMapperNrom = 0,   // the reference's only board
+    kMapperUxrom = 2,  // 16 KB PRG bank at $8000 selected by writes to $8000-$FFFF; last bank fixed at $C000
+    kMapperCnrom = 3,  // 8 KB CHR bank selected by writes to $8000-$FFFF
+};
+
+// Bank registers of one env (UxROM, CNROM); zero on every reset.  Writes have
+// bus conflicts: the value written is ANDed with the PRG byte at the address.
+typedef struct MapperState {
+    uint8_t prg_bank;       // UxROM: 16 KB bank at $8000-$BFFF
+    uint8_t chr_bank;       // CNROM: 8 KB CHR bank
+    uint8_t snap_chr_bank;  // CNROM: chr_bank latched at vblank (the presentation snapshot renders with it)
+    uint8_t pad;
+} MapperState;
 
 // Done predicates.
 enum {
@@ -150,6 +167,12 @@ typedef struct BatchView {
     // interleaved placements: the step kernel's working copy of RAM, per CTA
     // [512 words][lanes][4 bytes] (NULL otherwise)
     uint8_t* ram_work;
+    // cartridge board (kMapper*): bank registers per env, the whole PRG ROM
+    // (prg above is the 32 KB window at $8000 at power-on: for UxROM bank 0 and
+    // the fixed last bank), bank counts
+    MapperState* mstate;
+    const uint8_t* prg_rom;
+    uint32_t mapper, prg_banks, chr_banks, pad3;
 } BatchView;
 
 #ifdef __cplusplus

@@ -33,7 +33,8 @@ FIELD_DTYPES: dict[str, tuple[np.dtype, tuple[int, ...]]] = {
     "stat_budget_hits": (np.uint32, ()), "ram": (np.uint8, (2048,)), "prg_ram": (np.uint8, (8192,)),
     "nt": (np.uint8, (2048,)), "pal": (np.uint8, (32,)), "oam": (np.uint8, (256,)),
     "snap_oam": (np.uint8, (256,)), "snap_nt": (np.uint8, (2048,)), "snap_pal": (np.uint8, (32,)),
-    "ram_touch": (np.uint64, ()),
+    "ram_touch": (np.uint64, ()), "prg_bank": (np.uint8, ()), "chr_bank": (np.uint8, ()),
+    "snap_chr_bank": (np.uint8, ()),
 }
 
 _u8p = ctypes.POINTER(ctypes.c_uint8)

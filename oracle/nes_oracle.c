@@ -122,6 +122,7 @@ typedef struct {
     uint32_t stat_frames, stat_budget_hits;
     uint8_t ram[2048], prg_ram[8192], nt[2048], pal[32], oam[256];
     uint8_t snap_oam[256], snap_nt[2048], snap_pal[32];
+    uint8_t prg_bank, chr_bank, snap_chr_bank; /* EXTENSION: UxROM / CNROM bank registers */
     uint64_t ram_touch; /* MEASUREMENT: 32-byte RAM sectors read or written during the last env-step */
 } env_t;
 
@@ -144,6 +145,8 @@ struct nes_oracle {
     uint8_t *chr;
     uint32_t chr_size;
     uint8_t horizontal; /* nametable arrangement: 0 vertical, 1 horizontal */
+    uint32_t mapper, prg_banks, chr_banks; /* EXTENSION: 0 NROM, 2 UxROM, 3 CNROM */
+    uint8_t *prg_rom;                      /* the whole PRG ROM (UxROM banks) */
     snap_t *snaps;
     uint32_t nsnap;
     uint8_t *env_to_level;
@@ -196,13 +199,32 @@ static int parse_ines(nes_oracle *o, const uint8_t *b, size_t len) {
     size_t off = 16 + ((f6 & 0x04) ? 512 : 0);
     size_t prg = (size_t)prg_banks * 16384, chr = (size_t)chr_banks * 8192;
     if (len < off + prg + chr) { strcpy(g_err, "iNES data is truncated for declared PRG/CHR sizes"); return -1; }
-    if (mapper != 0 || (prg_banks != 1 && prg_banks != 2)) {
-        strcpy(g_err, "CUDA console mode currently supports mapper 0/NROM ROMs"); return -1;
+    /* EXTENSION: the reference accepts NROM only; this checker also restates
+     * UxROM (mapper 2, power-of-two 16 KB PRG banks, the last one fixed at
+     * $C000) and CNROM (mapper 3, 16/32 KB PRG, power-of-two 8 KB CHR banks). */
+    int pow2_prg = prg_banks && !(prg_banks & (prg_banks - 1)), pow2_chr = chr_banks && !(chr_banks & (chr_banks - 1));
+    int nrom = mapper == 0 && (prg_banks == 1 || prg_banks == 2);
+    int uxrom = mapper == 2 && prg_banks >= 2 && prg_banks <= 16 && pow2_prg && chr_banks <= 1;
+    int cnrom = mapper == 3 && (prg_banks == 1 || prg_banks == 2) && chr_banks <= 4 && pow2_chr;
+    if (!nrom && !uxrom && !cnrom) {
+        strcpy(g_err, "supported cartridges: mapper 0/NROM, 2/UxROM and 3/CNROM"); return -1;
     }
     if (f6 & 0x08) { strcpy(g_err, "four-screen nametables are not supported"); return -1; }
-    o->prg_size = (uint32_t)prg;
-    o->prg = malloc(prg);
-    memcpy(o->prg, b + off, prg);
+    o->mapper = mapper;
+    o->prg_banks = prg_banks;
+    o->chr_banks = chr_banks;
+    o->prg_rom = malloc(prg);
+    memcpy(o->prg_rom, b + off, prg);
+    if (uxrom) { /* the fixed window: bank 0 at $8000, the last bank at $C000 */
+        o->prg_size = 32768;
+        o->prg = malloc(32768);
+        memcpy(o->prg, b + off, 16384);
+        memcpy(o->prg + 16384, b + off + prg - 16384, 16384);
+    } else {
+        o->prg_size = (uint32_t)prg;
+        o->prg = malloc(prg);
+        memcpy(o->prg, b + off, prg);
+    }
     o->chr_size = (uint32_t)chr;
     o->chr = chr ? malloc(chr) : NULL;
     if (chr) memcpy(o->chr, b + off + prg, chr);
@@ -298,9 +320,14 @@ static uint16_t mirror_nt(const nes_oracle *o, uint16_t a) {
     return i & 0x07FF;
 }
 /* batch_bus.cuh:55-95 (live state) and batch_render.cuh:104-121 (any view). */
-static uint8_t ppu_mem_read(const nes_oracle *o, const uint8_t *nt, const uint8_t *pal, uint16_t a) {
+static uint8_t ppu_mem_read(const nes_oracle *o, uint8_t chr_bank, const uint8_t *nt, const uint8_t *pal,
+                            uint16_t a) {
     a &= 0x3FFF;
-    if (a < 0x2000) return (o->chr && o->chr_size) ? o->chr[a % o->chr_size] : 0;
+    if (a < 0x2000) {
+        /* EXTENSION: CNROM selects an 8 KB CHR bank */
+        uint32_t off = o->mapper == 3 ? (uint32_t)chr_bank * 8192u : 0u;
+        return (o->chr && o->chr_size) ? o->chr[(off + a) % o->chr_size] : 0;
+    }
     if (a < 0x3F00) {
         if (a >= 0x3000) a -= 0x1000;
         return nt[mirror_nt(o, a)];
@@ -341,6 +368,15 @@ static void oam_dma(env_t *e, uint8_t page) {
     e->pending_dma += 513;
 }
 
+/* PRG ROM at $8000-$FFFF (batch_bus.cuh:24-33); EXTENSION: UxROM maps the
+ * env's bank at $8000-$BFFF. */
+static uint8_t prg_read(const nes_oracle *o, const env_t *e, uint16_t a) {
+    if (o->mapper == 2 && a < 0xC000) return o->prg_rom[(uint32_t)e->prg_bank * 0x4000u + (a & 0x3FFF)];
+    uint32_t i = (uint32_t)(a - 0x8000);
+    i &= (o->prg_size == 16384) ? 0x3FFF : 0x7FFF;
+    return o->prg[i];
+}
+
 /* batch_bus.cuh:156-213 */
 static uint8_t bus_read(const nes_oracle *o, env_t *e, uint16_t a) {
     if (a < 0x2000) { TOUCH(e, a); return e->ram[a & 0x7FF]; }
@@ -359,11 +395,11 @@ static uint8_t bus_read(const nes_oracle *o, env_t *e, uint16_t a) {
             uint16_t pa = e->v & 0x3FFF;
             uint8_t v;
             if (pa >= 0x3F00) {
-                v = ppu_mem_read(o, e->nt, e->pal, pa);
-                e->read_buffer = ppu_mem_read(o, e->nt, e->pal, (uint16_t)(pa - 0x1000));
+                v = ppu_mem_read(o, e->chr_bank, e->nt, e->pal, pa);
+                e->read_buffer = ppu_mem_read(o, e->chr_bank, e->nt, e->pal, (uint16_t)(pa - 0x1000));
             } else {
                 v = e->read_buffer;
-                e->read_buffer = ppu_mem_read(o, e->nt, e->pal, pa);
+                e->read_buffer = ppu_mem_read(o, e->chr_bank, e->nt, e->pal, pa);
             }
             e->v = (uint16_t)(e->v + ((e->ppu_ctrl & 0x04) ? 32 : 1));
             e->open_bus = v;
@@ -374,11 +410,7 @@ static uint8_t bus_read(const nes_oracle *o, env_t *e, uint16_t a) {
     if (a == 0x4016) return read_controller(e);
     if (a == 0x4017) return 0x41;
     if (a >= 0x6000 && a < 0x8000) return e->prg_ram[a - 0x6000];
-    if (a >= 0x8000) {
-        uint32_t i = (uint32_t)(a - 0x8000);
-        i &= (o->prg_size == 16384) ? 0x3FFF : 0x7FFF;
-        return o->prg[i];
-    }
+    if (a >= 0x8000) return prg_read(o, e, a);
     return 0;
 }
 
@@ -434,6 +466,11 @@ static void bus_write(const nes_oracle *o, env_t *e, uint16_t a, uint8_t v) {
         return;
     }
     if (a >= 0x6000 && a < 0x8000) e->prg_ram[a - 0x6000] = v;
+    if (a >= 0x8000 && o->mapper) { /* EXTENSION: board register, with the bus conflict of the ROM byte */
+        v &= prg_read(o, e, a);
+        if (o->mapper == 2) e->prg_bank = (uint8_t)(v & (o->prg_banks - 1));
+        else e->chr_bank = (uint8_t)(v & (o->chr_banks - 1));
+    }
 }
 
 /* ------------------------------------------------------------------------ */
@@ -688,6 +725,7 @@ static uint32_t ppu_settle(env_t *e, uint32_t ppu_cycles) {
             memcpy(e->snap_oam, e->oam, 256);
             memcpy(e->snap_nt, e->nt, 2048);
             memcpy(e->snap_pal, e->pal, 32);
+            e->snap_chr_bank = e->chr_bank;
         }
         if (CROSSED(PRERENDER_DOT)) {
             set_vblank(e, 0);
@@ -789,10 +827,12 @@ static void warm_reset(const nes_oracle *o, env_t *e, uint32_t env) {
 
 static void reset_env(const nes_oracle *o, env_t *e, uint32_t env) {
     if (o->nsnap) warm_reset(o, e, env); else cold_reset(o, e);
+    e->prg_bank = e->chr_bank = 0; /* EXTENSION: board registers; the snapshot's CHR bank survives */
 }
 
 /* cuda_module.cu:1443-1463 */
 static void seed_presentation(env_t *e) {
+    e->snap_chr_bank = e->chr_bank;
     memcpy(e->snap_nt, e->nt, 2048);
     memcpy(e->snap_pal, e->pal, 32);
     memcpy(e->snap_oam, e->oam, 256);
@@ -920,7 +960,7 @@ nes_oracle *oracle_create(uint32_t num_envs, uint32_t frameskip, const uint8_t *
 
 void oracle_destroy(nes_oracle *o) {
     if (!o) return;
-    free(o->prg); free(o->chr); free(o->snaps); free(o->env_to_level); free(o->env);
+    free(o->prg); free(o->prg_rom); free(o->chr); free(o->snaps); free(o->env_to_level); free(o->env);
     free(o);
 }
 
@@ -979,7 +1019,7 @@ void oracle_poke_ram(nes_oracle *o, uint16_t address, uint8_t value) {
 /* Renderer: cpp/include/nesle/cuda/batch_render.cuh:123-434 over the
  * presentation-snapshot views resolved as in :333-370.                       */
 /* ------------------------------------------------------------------------ */
-typedef struct { const uint8_t *nt, *pal, *oam; uint8_t sx, sy, ctrl, mask; } view_t;
+typedef struct { const uint8_t *nt, *pal, *oam; uint8_t sx, sy, ctrl, mask, chr_bank; } view_t;
 
 /* NES master palette (2C02), 64 RGB triples, as in batch_render.cuh:23-40. */
 static const uint8_t kRgb[64][3] = {
@@ -995,14 +1035,14 @@ static const uint8_t kRgb[64][3] = {
 
 /* batch_render.cuh:123-131 */
 static uint8_t pal_entry(const nes_oracle *o, const view_t *v, uint16_t idx) {
-    uint8_t c = ppu_mem_read(o, v->nt, v->pal, (uint16_t)(0x3F00 + idx));
+    uint8_t c = ppu_mem_read(o, v->chr_bank, v->nt, v->pal, (uint16_t)(0x3F00 + idx));
     if (v->mask & 1) c &= 0x30;
     return c & 0x3F;
 }
 /* batch_render.cuh:148-159 */
 static uint8_t pattern_px(const nes_oracle *o, const view_t *v, uint16_t tile_base, int fx, int fy) {
-    uint8_t lo = ppu_mem_read(o, v->nt, v->pal, (uint16_t)(tile_base + fy));
-    uint8_t hi = ppu_mem_read(o, v->nt, v->pal, (uint16_t)(tile_base + fy + 8));
+    uint8_t lo = ppu_mem_read(o, v->chr_bank, v->nt, v->pal, (uint16_t)(tile_base + fy));
+    uint8_t hi = ppu_mem_read(o, v->chr_bank, v->nt, v->pal, (uint16_t)(tile_base + fy + 8));
     int bit = 7 - fx;
     return (uint8_t)(((lo >> bit) & 1) | (((hi >> bit) & 1) << 1));
 }
@@ -1018,10 +1058,10 @@ static uint8_t bg_color(const nes_oracle *o, const view_t *v, int x, int y) {
     unsigned ntx = ((base & 1) + wx / 256) & 1;
     uint16_t ntb = (uint16_t)(0x2000 + (ntx | (nty << 1)) * 0x400);
     uint16_t pb = (v->ctrl & 0x10) ? 0x1000 : 0;
-    uint8_t tile = ppu_mem_read(o, v->nt, v->pal, (uint16_t)(ntb + cy * 32 + cx));
+    uint8_t tile = ppu_mem_read(o, v->chr_bank, v->nt, v->pal, (uint16_t)(ntb + cy * 32 + cx));
     uint8_t c = pattern_px(o, v, (uint16_t)(pb + tile * 16), (int)fx, (int)fy);
     if (c == 0) return 0;
-    uint8_t at = ppu_mem_read(o, v->nt, v->pal, (uint16_t)(ntb + 0x3C0 + (cy / 4) * 8 + cx / 4));
+    uint8_t at = ppu_mem_read(o, v->chr_bank, v->nt, v->pal, (uint16_t)(ntb + 0x3C0 + (cy / 4) * 8 + cx / 4));
     int shift = ((cy & 2) << 1) | (cx & 2);
     return pal_entry(o, v, (uint16_t)(((at >> shift) & 3) * 4 + c));
 }
@@ -1052,7 +1092,7 @@ void oracle_render(const nes_oracle *o, uint8_t *index, uint8_t *rgb, uint8_t *g
         const env_t *e = &o->env[env];
         /* batch_render.cuh:333-370 */
         view_t play = {e->snap_nt, e->snap_pal, e->snap_oam, e->snap_sx_end, e->snap_sy_end,
-                       e->snap_ctrl_end, e->snap_mask};
+                       e->snap_ctrl_end, e->snap_mask, e->snap_chr_bank};
         view_t hud = play;
         hud.sx = e->snap_sx_start; hud.sy = e->snap_sy_start; hud.ctrl = e->snap_ctrl_start;
         /* Rows above `split` use the frame-start view; the rest, the backdrop,
@@ -1144,6 +1184,7 @@ static const field_t kFields[] = {
     FLD(stat_instructions, 8), FLD(stat_frames, 4), FLD(stat_budget_hits, 4),
     FLD(ram, 2048), FLD(prg_ram, 8192), FLD(nt, 2048), FLD(pal, 32), FLD(oam, 256),
     FLD(snap_oam, 256), FLD(snap_nt, 2048), FLD(snap_pal, 32), FLD(ram_touch, 8),
+    FLD(prg_bank, 1), FLD(chr_bank, 1), FLD(snap_chr_bank, 1),
 };
 #undef FLD
 

@@ -208,3 +208,95 @@ def env_trace_snapshots(k: int = 8) -> list[bytes]:
         snaps.append(w.write_fcs(w.Snapshot(pc=_TRACE_LOOP, a=lvl, x=3 * lvl, cpu_ram=bytes(ram), ppu_ctrl=0x80,
                                             ppu_mask=0x1E)))
     return snaps
+
+
+# Cartridge boards beyond NROM (no counterpart in the reference, which is
+# NROM-only): UxROM (mapper 2) and CNROM (mapper 3).  Both select a bank by a
+# write to $8000-$FFFF whose value is ANDed with the ROM byte at that address
+# (bus conflict), so the programs write through a table of bank numbers.
+def board_image(mapper: int, prg: bytes, chr_rom: bytes, flags6: int = 0x01) -> bytes:
+    assert len(prg) % 16384 == 0 and len(chr_rom) % 8192 == 0
+    header = b"NES\x1a" + bytes([len(prg) // 16384, len(chr_rom) // 8192, flags6 | ((mapper & 0xF) << 4),
+                                 mapper & 0xF0]) + bytes(8)
+    return header + prg + chr_rom
+
+
+def _joypad_bits(n: int) -> list:
+    """Strobe the controller, then read n buttons into X: X = b0 | b1 << 1 | ..."""
+    lines = [("LDA", w.IMM, 1), ("STA", w.ABS, 0x4016), ("LDA", w.IMM, 0), ("STA", w.ABS, 0x4016),
+             ("LDX", w.IMM, 0), ("STX", w.ZP, 0x20)]
+    for k in range(n):
+        lines += [("LDA", w.ABS, 0x4016), ("AND", w.IMM, 1)]
+        lines += [("ASL", w.ACC)] * k
+        lines += [("ORA", w.ZP, 0x20), ("STA", w.ZP, 0x20)]
+    lines += [("LDX", w.ZP, 0x20)]
+    return lines
+
+
+def _uxrom_rom() -> bytes:
+    """64 KB UxROM: 4 switchable banks, each with a routine at $8000 that
+    stores its bank's signature (read from $8010) and counts its calls; the
+    fixed bank picks a bank from two joypad bits each pass (no conflict), then
+    writes $FF over a table byte holding 1 (conflict: bank 1), calling each."""
+    banks = []
+    for b in range(4):
+        bank = bytearray([0xEA]) * 16384
+        code = asm(0x8000, ("LDA", w.ABS, 0x8010), ("STA", w.ABS, 0x0310 + b), ("INC", w.ABS, 0x0320 + b),
+                   ("LDA", w.ABSY, 0x8011), ("STA", w.ZP, 0x30), ("RTS",))
+        bank[:len(code)] = code
+        bank[0x10] = 0xA0 + b
+        bank[0x11:0x15] = bytes([(0x11 * (b + 1) + 4 * j) & 0xFF for j in range(4)])
+        banks.append(bank)
+    fixed = banks[3]
+    table = 0xC100
+    main = asm(0xC000, ("LDA", w.IMM, 0x00), ("STA", w.ABS, 0x2000), ("LDY", w.IMM, 0x00),
+               *_joypad_bits(2), ("LDA", w.ABSX, table), ("STA", w.ABSX, table), ("JSR", w.ABS, 0x8000),
+               ("LDA", w.IMM, 0xFF), ("STA", w.ABS, table + 1), ("JSR", w.ABS, 0x8000),
+               ("INY",), ("TYA",), ("AND", w.IMM, 3), ("TAY",), ("INC", w.ABS, 0x0300), ("JMP", w.ABS, 0xC004))
+    fixed[0x4000 - 0x4000:len(main)] = main
+    fixed[0x100:0x104] = bytes([0, 1, 2, 3])
+    fixed[0x3FFA:0x3FFC] = struct.pack("<H", 0xC000)  # NMI (off)
+    fixed[0x3FFC:0x3FFE] = struct.pack("<H", 0xC000)
+    fixed[0x3FFE:0x4000] = struct.pack("<H", 0xC000)
+    return board_image(2, b"".join(bytes(x) for x in banks), bytes((i * 7) & 0xFF for i in range(8192)))
+
+
+def _cnrom_rom() -> bytes:
+    """32 KB PRG, 4 CHR banks of distinct patterns (CNROM).  Reset fills the
+    first nametable with a tile ramp and the palette, turns rendering and NMI
+    on; the main loop selects a CHR bank from two joypad bits, reads a
+    pattern byte back through $2006/$2007 into RAM and waits for vblank."""
+    prg = bytearray([0xEA]) * 32768
+    table = 0xE000
+    init = [("LDA", w.IMM, 0x00), ("STA", w.ABS, 0x2000), ("STA", w.ABS, 0x2001),
+            ("LDA", w.IMM, 0x3F), ("STA", w.ABS, 0x2006), ("LDA", w.IMM, 0x00), ("STA", w.ABS, 0x2006),
+            ("LDX", w.IMM, 0x00)]
+    pal = asm(0x8000, *init)
+    fill_pal = asm(0x8000 + len(pal), ("TXA",), ("ASL", w.ACC), ("ADC", w.IMM, 0x05), ("STA", w.ABS, 0x2007),
+                   ("INX",), ("CPX", w.IMM, 0x20), ("BNE", w.REL, 0xF5))
+    nt_start = asm(0x8000 + len(pal) + len(fill_pal), ("LDA", w.IMM, 0x20), ("STA", w.ABS, 0x2006),
+                   ("LDA", w.IMM, 0x00), ("STA", w.ABS, 0x2006), ("LDY", w.IMM, 0x04), ("LDX", w.IMM, 0x00))
+    base = 0x8000 + len(pal) + len(fill_pal) + len(nt_start)
+    fill_nt = asm(base, ("TXA",), ("STA", w.ABS, 0x2007), ("INX",), ("BNE", w.REL, 0xF9), ("DEY",),
+                  ("BNE", w.REL, 0xF6))
+    on = asm(base + len(fill_nt), ("LDA", w.IMM, 0x00), ("STA", w.ABS, 0x2005), ("STA", w.ABS, 0x2005),
+             ("LDA", w.IMM, 0x80), ("STA", w.ABS, 0x2000), ("LDA", w.IMM, 0x1E), ("STA", w.ABS, 0x2001))
+    head = base + len(fill_nt) + len(on)
+    loop = asm(head, *_joypad_bits(2), ("LDA", w.ABSX, table), ("STA", w.ABSX, table),
+               ("LDA", w.IMM, 0x00), ("STA", w.ABS, 0x2006), ("LDA", w.IMM, 0x10), ("STA", w.ABS, 0x2006),
+               ("LDA", w.ABS, 0x2007), ("LDA", w.ABS, 0x2007), ("STA", w.ABS, 0x0340), ("STX", w.ABS, 0x0341),
+               ("INC", w.ABS, 0x0342), ("LDA", w.IMM, 0x00), ("STA", w.ABS, 0x2005), ("STA", w.ABS, 0x2005),
+               ("JMP", w.ABS, head))
+    code = pal + fill_pal + nt_start + fill_nt + on + loop
+    prg[:len(code)] = code
+    prg[table - 0x8000:table - 0x8000 + 4] = bytes([0, 1, 2, 3])
+    prg[0x7000:0x7002] = bytes([0x40, 0x40])  # NMI: RTI
+    prg[0x7FFA:0x7FFC] = struct.pack("<H", 0xF000)
+    prg[0x7FFC:0x7FFE] = struct.pack("<H", 0x8000)
+    prg[0x7FFE:0x8000] = struct.pack("<H", 0xF000)
+    chr_rom = bytes(((i * (k + 3)) ^ (k * 0x55) ^ (i >> 4)) & 0xFF for k in range(4) for i in range(8192))
+    return board_image(3, bytes(prg), chr_rom)
+
+
+UXROM_ROM = _uxrom_rom()
+CNROM_ROM = _cnrom_rom()

@@ -30,7 +30,8 @@ struct HostBatch {
     std::vector<uint8_t> ram, prg_ram, nt, pal, oam, snap_nt, snap_pal, snap_oam, done, last_done, prg, chr;
     std::vector<float> rewards, last_rewards;
     std::vector<BankRecord> bank;
-    std::vector<uint8_t> bram, bprg, bnt, bpal, boam, e2l;
+    std::vector<uint8_t> bram, bprg, bnt, bpal, boam, e2l, prg_rom;
+    std::vector<MapperState> mstate;
     uint32_t fault = 0;
     bool global_ram = false;  // run the in-place (global-RAM) variant of the core
     bool hybrid = false;      // ... with one page in a separate slot (hybrid placement)
@@ -68,7 +69,11 @@ int host_create(const nesle_create_args* a, void** out) {
     h->snap_nt.assign(n * kNtBytes, 0); h->snap_pal.assign(n * kPalBytes, 0); h->snap_oam.assign(n * kOamBytes, 0);
     h->rewards.assign(n, 0.f); h->last_rewards.assign(n, 0.f); h->done.assign(n, 0); h->last_done.assign(n, 0);
     h->prg.resize(32768 + 16, 0);
-    for (size_t i = 0; i < 32768; ++i) h->prg[i] = cart.prg[i % cart.prg.size()];
+    const size_t last = cart.prg.size() - 16384;  // the kernels' window: UxROM bank 0 + fixed last bank
+    for (size_t i = 0; i < 32768; ++i)
+        h->prg[i] = cart.mapper == kMapperUxrom ? cart.prg[i < 16384 ? i : last + i - 16384] : cart.prg[i % cart.prg.size()];
+    h->prg_rom = cart.mapper == kMapperUxrom ? cart.prg : std::vector<uint8_t>(h->prg.begin(), h->prg.begin() + 32768);
+    h->mstate.assign(n, MapperState{});
     h->chr = cart.chr;
     h->bank.resize(k ? k : 1);
     h->bram.resize(k * kRamBytes); h->bprg.resize(k * kPrgRamBytes); h->bnt.resize(k * kNtBytes);
@@ -105,6 +110,8 @@ int host_create(const nesle_create_args* a, void** out) {
     v.max_instructions = a->max_instructions_per_frame ? a->max_instructions_per_frame : 200000u;
     v.done_mode = a->done_mode; v.done_a = a->done_a; v.done_b = a->done_b; v.env_offset = a->env_offset;
     v.seed = a->seed;
+    v.mapper = cart.mapper; v.prg_banks = cart.prg_banks; v.chr_banks = cart.chr_banks;
+    v.mstate = h->mstate.data(); v.prg_rom = h->prg_rom.data();
     for (uint32_t e = 0; e < n; ++e) {
         EnvRecord& r = h->rec[e];
         r.episode = 0;
@@ -180,6 +187,8 @@ void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) 
         c.zp = nullptr;
         c.zslots = 0;
         c.zpage = 0;
+        c.prg_lo = h->v.mapper == kMapperUxrom ? 0xC000u : 0x8000u;
+        c.prg_writes = h->v.mapper != kMapperNrom;
         uint32_t zp[64];  // hybrid placement: this env's slot page as one lane of words
         if (h->hybrid) {
             c.zpage = h->slot_page;
@@ -292,6 +301,13 @@ int host_copy_field(void* p, const char* name, void* out, uint64_t bytes) {
     RF("pending_dma", pending_dma) RF("episode", episode) RF("status", status)
     RF("stat_instructions", stat_instructions) RF("stat_frames", stat_frames) RF("stat_budget_hits", stat_budget_hits)
 #undef RF
+    const char* board_fields[] = {"prg_bank", "chr_bank", "snap_chr_bank"};
+    for (uint32_t k = 0; k < 3; ++k)
+        if (f == board_fields[k]) {
+            if (bytes != n) { g_err = "wrong size"; return NESLE_ERR_INVALID; }
+            for (uint64_t e = 0; e < n; ++e) static_cast<uint8_t*>(out)[e] = reinterpret_cast<const uint8_t*>(&h->mstate[e])[k];
+            return NESLE_OK;
+        }
     g_err = "unknown field " + f;
     return NESLE_ERR_INVALID;
 }

@@ -218,3 +218,28 @@ def test_controller_protocol_matches_checker(cls):
         o.step(a, auto_reset=False)
         h.step(a, auto_reset=False)
         assert_same(o, h, label="controller")
+
+
+BOARD_FIELDS = STATE_FIELDS + ("prg_bank", "chr_bank", "snap_chr_bank")
+
+
+@pytest.mark.parametrize("rom", ["UXROM_ROM", "CNROM_ROM"])
+@pytest.mark.parametrize("core", [HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreV1, HostCoreHybridV1])
+def test_boards_match_checker(rom, core):
+    """UxROM and CNROM (bank writes with bus conflicts, code and data in the
+    switchable PRG bank, banked CHR read through $2007 and rendered from the
+    bank latched at vblank): every field every step, frames at the end."""
+    image = getattr(kat, rom)
+    n = 12
+    o = Oracle(n, 2, image)
+    h = core(n, 2, image)
+    rng = np.random.default_rng(3)
+    for s in range(8):
+        a = rng.integers(0, 256, n, dtype=np.uint8)
+        o.step(a, auto_reset=False)
+        h.step(a, auto_reset=False)
+        assert_same(o, h, BOARD_FIELDS, f"{rom} step {s}")
+    ro, rh = o.render(), h.render()
+    for k in ("index", "rgb", "gray84"):
+        np.testing.assert_array_equal(ro[k], rh[k], err_msg=k)
+    assert len(np.unique(o.get("prg_bank" if rom == "UXROM_ROM" else "chr_bank"))) > 1

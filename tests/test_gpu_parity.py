@@ -325,3 +325,49 @@ def test_controller_protocol_matches_checker(variant, monkeypatch):
         o.step(a, auto_reset=False)
         g.step(a, auto_reset=False)
         assert_same(o, g, label=f"controller {variant}")
+
+
+BOARD_FIELDS = STATE_FIELDS + ("prg_bank", "chr_bank", "snap_chr_bank")
+
+
+@pytest.mark.parametrize("rom", ["UXROM_ROM", "CNROM_ROM"])
+@pytest.mark.parametrize("variant", ["shared", "global", "hybrid"])
+def test_boards_match_checker(rom, variant, monkeypatch):
+    """UxROM and CNROM cartridges (no counterpart in the reference): every field
+    every step against the checker, env resets through the mask, a saved state
+    loaded into another env, and all three frame formats."""
+    monkeypatch.setenv("NESLE_STEP_KERNEL", variant)
+    image = getattr(kat, rom)
+    n = 100
+    o = Oracle(n, 2, image)
+    g = GpuCore(n, 2, image)
+    rng = np.random.default_rng(11)
+    for s in range(8):
+        a = rng.integers(0, 256, n, dtype=np.uint8)
+        o.step(a, auto_reset=False)
+        g.step(a, auto_reset=False)
+        assert_same(o, g, BOARD_FIELDS, f"{rom} {variant} step {s}")
+        if s == 4:
+            mask = (np.arange(n) % 5 == 0).astype(np.uint8)
+            o.reset_envs(mask)
+            g.reset_envs(mask)
+            assert_same(o, g, BOARD_FIELDS, f"{rom} {variant} after reset_envs")
+    ro, rg = o.render(), g.render()
+    for k in ("index", "rgb", "gray84"):
+        np.testing.assert_array_equal(ro[k], rg[k], err_msg=k)
+    w_ = g.window(np.arange(n))
+    blob = np.zeros((1, _lib.STATE_BYTES), np.uint8)
+    idx = np.array([7], np.uint32)
+    _lib.check(g.lib.nesle_save_states(g._h, idx.ctypes.data, 1, 0, blob.ctypes.data, 0, None))
+    dst = np.array([8], np.uint32)
+    _lib.check(g.lib.nesle_load_states(g._h, dst.ctypes.data, 1, 0, blob.ctypes.data, 0, None))
+    for f in ("prg_bank", "chr_bank", "snap_chr_bank", "pc", "ram"):
+        got = g.get(f)
+        np.testing.assert_array_equal(got[8], got[7], err_msg=f"{f} after loading env 7's state into env 8")
+    assert w_["pc"].shape == (n,)
+
+
+def test_unsupported_boards_are_rejected():
+    bad = kat.board_image(1, bytes(32768), bytes(8192))  # MMC1
+    with pytest.raises(ValueError, match="supported cartridges"):
+        GpuCore(4, 1, bad)
