@@ -43,7 +43,7 @@ typedef struct nesle_create_args {
     int device;                           /* CUDA device ordinal */
     uint32_t num_envs;                    /* envs on this device */
     uint32_t frameskip;                   /* frames per env-step (> 0) */
-    const uint8_t* rom;                   /* iNES image (mapper 0, 16/32 KB PRG) */
+    const uint8_t* rom;                   /* iNES image: mapper 0 NROM (the reference's only board), 2 UxROM, 3 CNROM */
     size_t rom_len;
     const uint8_t* const* snapshots;      /* uncompressed FCS save states, may be NULL */
     const size_t* snapshot_lens;

@@ -445,10 +445,14 @@ class CudaBatch:
 
     @property
     def step_kernel_placement(self) -> str:
-        """Where the step kernel keeps env RAM: "shared" (staged in shared memory),
-        "global" (in place), "hybrid" (in place, zero page in shared memory),
-        "hybrid-stack" (stack page instead), and the "-async" forms of the in-place
-        ones (operands loaded ahead asynchronously)."""
+        """Where the step kernel keeps env RAM (NESLE_STEP_KERNEL overrides the
+        choice at construction): "shared" (the whole row staged in shared memory;
+        the default for small batches), "interleaved" (zero page in shared memory,
+        the rest in an env-interleaved working copy in device memory; the default
+        for large ones), "global" (in place), "hybrid" (in place, zero page in
+        shared memory; UxROM / CNROM batches above the shared size),
+        "hybrid-stack" (stack page instead), and the "-async" / "-preload" forms
+        (operands loaded ahead), kept as measured alternatives."""
         info = _lib.Info()
         self._check(self._lib.nesle_get_info(self._h, ctypes.byref(info)))
         return _lib.PLACEMENTS[info.step_placement]

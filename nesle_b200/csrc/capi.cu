@@ -321,26 +321,26 @@ static int create_impl(const nesle_create_args* a, nesle_batch* b) {
     // (kStepSlots envs per SM per wave) the RAM is staged in shared memory: with
     // few warps per SM the latency of each env's instruction chain decides, and
     // shared memory has the shorter one (B200, config-4 workload: 185k vs 77k
-    // env-steps/s at 2,048 envs, 740k vs 592k at 16,384; in place wins from
-    // 32,768 on).  Larger batches keep RAM in place, every env resident, with
-    // the zero page in shared memory (hybrid: config 4 at 65,536 envs 2.10 M vs
-    // 1.90 M all in place; config 2 loses 2%, config 3's step 7%).
-    // NESLE_STEP_KERNEL=shared|global|hybrid|hybrid-stack overrides.
+    // env-steps/s at 2,048 envs, 740k vs 592k at 16,384).  Larger batches keep
+    // every env resident with the zero page in shared memory and the rest of RAM
+    // in the env-interleaved working copy (B200, 65,536 envs: config 4 2.36 M
+    // env-steps/s against 2.27 M in place with the zero page staged, config 2
+    // 3.29 M against 3.26 M; config 3's step is 4% slower than in place).
+    // NESLE_STEP_KERNEL=<placement name> overrides.
     int sms = 0;
     CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, a->device), "SM count");
-    b->step_variant = b->n <= 2u * (uint32_t)sms * kStepSlots ? kStepSharedRam : kStepHybridRam;
+    b->step_variant = b->n <= 2u * (uint32_t)sms * kStepSlots ? kStepSharedRam : kStepInterleaved;
     if (const char* sv = getenv("NESLE_STEP_KERNEL")) {
-        if (strcmp(sv, "global") == 0) b->step_variant = kStepGlobalRam;
-        else if (strcmp(sv, "shared") == 0) b->step_variant = kStepSharedRam;
-        else if (strcmp(sv, "hybrid") == 0) b->step_variant = kStepHybridRam;
-        else if (strcmp(sv, "hybrid-stack") == 0) b->step_variant = kStepHybridStackRam;
-        else if (strcmp(sv, "global-async") == 0) b->step_variant = kStepGlobalAsync;
-        else if (strcmp(sv, "hybrid-async") == 0) b->step_variant = kStepHybridAsync;
-        else if (strcmp(sv, "interleaved") == 0) b->step_variant = kStepInterleaved;
-        else if (strcmp(sv, "interleaved-async") == 0) b->step_variant = kStepInterleavedAsync;
-        else if (strcmp(sv, "global-preload") == 0) b->step_variant = kStepGlobalPreload;
-        else if (strcmp(sv, "hybrid-preload") == 0) b->step_variant = kStepHybridPreload;
-        else if (strcmp(sv, "interleaved-preload") == 0) b->step_variant = kStepInterleavedPreload;
+        // Names in kStep* order (the Python mirror's PLACEMENTS).
+        static const char* const kNames[] = {"shared", "global", "hybrid", "hybrid-stack", "global-async",
+                                             "hybrid-async", "interleaved", "interleaved-async",
+                                             "global-preload", "hybrid-preload", "interleaved-preload"};
+        static_assert(sizeof(kNames) / sizeof(kNames[0]) == kStepInterleavedPreload + 1, "placement names");
+        int found = -1;
+        for (int i = 0; i <= kStepInterleavedPreload; ++i)
+            if (strcmp(sv, kNames[i]) == 0) found = i;
+        if (found < 0) return fail(NESLE_ERR_INVALID, std::string("NESLE_STEP_KERNEL: unknown placement '") + sv + "'");
+        b->step_variant = found;
     }
     b->board = cart.mapper != kMapperNrom;
     if (b->board && b->step_variant != kStepSharedRam && b->step_variant != kStepGlobalRam)

@@ -36,7 +36,17 @@ __constant__ uint8_t kPaletteRgb[192] = NESLE_PALETTE_RGB;
 // (NESLE_STEP_KERNEL=shared forces it); larger batches use the in-place kernel.
 // --------------------------------------------------------------------------
 constexpr uint32_t kPrgSmem = 32768 + 16;  // +16: the two-word fetch at $FFFC-$FFFD reads one word past the ROM
-constexpr uint32_t kDecSmem = NESLE_V2 ? 256 * sizeof(Entry2) : 256 * sizeof(Entry);  // the table a kernel stages
+constexpr uint32_t kDecSmem = NESLE_V2 ? sizeof(EntryTable2) : 256 * sizeof(Entry);  // the table a kernel stages
+
+// Execution-entry quarters the v2 datapath prefetches one iteration ahead, per
+// placement.  B200, env-steps/s with 0 / 1 / 2 quarters: shared RAM, 2,048
+// envs of config 2: 240 / 247 / 244 k; hybrid, 65,536 envs of config 4:
+// 2.27 / 2.27 / 2.18 M (2 spills), config 2: 3.26 / 3.15 / 3.13 M;
+// interleaved, config 4: 2.31 / 2.34 / 2.36 M, config 2: 3.37 / 3.35 / 3.29 M.
+// Config 4 is the benchmark workload.
+constexpr uint32_t kEarlyShared = 1;
+constexpr uint32_t kEarlyInPlace = 0;
+constexpr uint32_t kEarlyInterleaved = 2;
 
 // Stages the execution entries of the datapath the kernel runs (v2 when
 // kV2) into shared memory at `dst`.
@@ -96,7 +106,7 @@ step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
     c.zpage = 0;
     c.prg = s_prg;
     c.dec = s_dec;
-    c.dec2 = reinterpret_cast<const Entry2*>(s_dec);
+    c.dec2 = reinterpret_cast<const EntryQuad*>(s_dec);
     c.view = vp;
     c.env = env;
     c.frameskip = v.frameskip;
@@ -113,7 +123,7 @@ step_kernel(const BatchView* __restrict__ vp, const uint8_t* __restrict__ act8,
     const uint8_t action = act64 ? (uint8_t)(act64[env] & 0xFF) : act8[env];
     float reward;
     uint8_t done;
-    if (NESLE_V2) run_env_step_v2<true>(c, rec, action, reward, done);
+    if (NESLE_V2) run_env_step_v2<true, kEarlyShared>(c, rec, action, reward, done);
     else run_env_step(c, rec, action, reward, done);
 
     uint4* dst = reinterpret_cast<uint4*>(v.ram + (size_t)env * kRamBytes);
@@ -282,7 +292,7 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
         }
         c.prg = s_prg;
         c.dec = s_dec;
-        c.dec2 = reinterpret_cast<const Entry2*>(s_dec);
+        c.dec2 = reinterpret_cast<const EntryQuad*>(s_dec);
         c.view = vp;
         c.env = env;
         c.frameskip = v.frameskip;
@@ -310,7 +320,7 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
             DevicePreload A;
             run_env_step_async(c, rec, action, reward, done, A);
         } else if (kV2) {
-            run_env_step_v2<false>(c, rec, action, reward, done);
+            run_env_step_v2<false, kInterleave ? kEarlyInterleaved : kEarlyInPlace>(c, rec, action, reward, done);
         } else {
             run_env_step<false>(c, rec, action, reward, done);
         }

@@ -456,7 +456,7 @@ NESLE_HD void store_lane(const Lane& L, EnvRecord& r) {
 // Memory context of one lane: RAM slot in the interleaved shared array, the
 // shared PRG/decode copies, and the env's rows of the global byte arrays.
 // ---------------------------------------------------------------------------
-struct Entry2;  // nes_v2.cuh
+struct EntryQuad;  // nes_v2.cuh
 
 struct Ctx {
     uint8_t* ram;         // &smem_ram[slot * 4]; byte a at ram[(a & 0x7FC) * slots + (a & 3)]
@@ -466,7 +466,7 @@ struct Ctx {
     uint32_t zpage;       // RAM page held in the slot: 0x000 (zero page) or 0x100 (stack)
     const uint8_t* prg;   // 32 KB (shared)
     const Entry* dec;     // execution entries (shared)
-    const Entry2* dec2;   // v2 execution entries (shared), when the kernel runs the v2 datapath
+    const EntryQuad* dec2;  // v2 execution entries, quad-major (shared), when the kernel runs the v2 datapath
     const BatchView* view;
     uint32_t env;
     uint32_t frameskip;   // copies of view fields read on every iteration

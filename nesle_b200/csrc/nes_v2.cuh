@@ -17,9 +17,14 @@
 //    which the integer datapath otherwise leaves idle); the shifter yields a
 //    9-bit value with the shifted-out bit at bit 8, like the adder's carry, so
 //    one carry extraction serves both units;
-//  * only the next instruction's three bytes are prefetched (one register);
-//    its entry is loaded at the top of its own iteration, so the prefetch
-//    costs no register moves across the loop's back edge.
+//  * the next instruction's three bytes are prefetched one iteration ahead,
+//    and with them, per kernel, the first one or two 16-byte quarters of its
+//    entry (the fields the next-PC and address stages read first); the rest
+//    (ALU, flags, write-back) is loaded at the top of its own iteration, where
+//    the address stage hides its latency;
+//  * the table is stored quad-major (four 16-byte quarters, each an array over
+//    the 256 opcodes), so lanes of one warp loading different opcodes spread
+//    over all 32 banks instead of colliding on a 64-byte stride.
 //
 // The header compiles as plain C++ too (the host unit-test build), like
 // nes_core.cuh.
@@ -50,25 +55,30 @@ NESLE_HD uint32_t prmt(uint32_t x, uint32_t y, uint32_t s) {
 }
 
 // ---------------------------------------------------------------------------
-// Execution entry v2.
-//   w0  flags (X_*), length at bits 16-17, base cycles at bits 24-27
-//   w1  PRMT selector of the index byte of R (X, Y, SP or zero) | of the
-//       (zp,X) pointer offset (X or zero) << 16
-//   w2  base mask applied to the operand word (0xFF zero page, 0xFFFF absolute)
-//   w3  base increment (1 for stack pulls)
-//   w4  address wrap (0xFF zero page and stack, 0xFFFF otherwise)
-//   w5  address OR (0x100 for the stack)
-//   w6  PRMT selector of operand A over {R, m | (P|$30) << 8}
-//   w7  operand B multiplier (0, 1, -1): B = m * w7 + w8
-//   w8  operand B addend (0, 0xFF; plus 1 where the carry-in is a constant 1)
-//   w9  carry-in multiplier (carry-in = C * w9)
-//   w10 adder result mask (0x1FF: the sum with its carry at bit 8)
-//   w11 AND mask | XOR mask << 8 | shifter mask << 16 (0x1FF, carry at bit 8)
-//   w12 P keep mask | computed mask << 8 | set bits << 16 | from-result mask << 24
-//   w13 branch value (bit 8 set for non-branches: never taken)
-//   w14 branch flag mask (with bit 8) | SP delta byte << 24 (0x01, 0xFF)
-//   w15 register write mask over R = A | X<<8 | Y<<16 | SP<<24
+// Execution entry v2 (word index: contents).  Words 0-7 are the early half.
+//   E_FLAGS  flags (X_*), length at bits 16-17, base cycles at bits 24-27
+//   E_SELIDX PRMT selector of the index byte of R (X, Y, SP or zero) | of the
+//            (zp,X) pointer offset (X or zero) << 16
+//   E_BRVAL  branch value (bit 8 set for non-branches: never taken)
+//   E_BRMASK branch flag mask (with bit 8) | SP delta byte << 24 (0x01, 0xFF)
+//   E_BASEM  base mask applied to the operand word (0xFF zero page, 0xFFFF absolute)
+//   E_ADDK   base increment (1 for stack pulls)
+//   E_WRAP   address wrap (0xFF zero page and stack, 0xFFFF otherwise)
+//   E_ORV    address OR (0x100 for the stack)
+//   E_SELA   PRMT selector of operand A over {R, m | (P|$30) << 8}
+//   E_BMUL   operand B multiplier (0, 1, -1): B = m * E_BMUL + E_BADD
+//   E_BADD   operand B addend (0, 0xFF; plus 1 where the carry-in is a constant 1)
+//   E_CINM   carry-in multiplier (carry-in = C * E_CINM)
+//   E_SUMM   adder result mask (0x1FF: the sum with its carry at bit 8)
+//   E_LOGIC  AND mask | XOR mask << 8 | shifter mask << 16 (0x1FF, carry at bit 8)
+//   E_PMASK  P keep mask | computed mask << 8 | set bits << 16 | from-result mask << 24
+//   E_WMASK  register write mask over R = A | X<<8 | Y<<16 | SP<<24
 // ---------------------------------------------------------------------------
+enum : uint32_t {
+    E_FLAGS = 0, E_SELIDX, E_BRVAL, E_BRMASK, E_BASEM, E_ADDK, E_WRAP, E_ORV,
+    E_SELA, E_BMUL, E_BADD, E_CINM, E_SUMM, E_LOGIC, E_PMASK, E_WMASK,
+};
+
 enum : uint32_t {
     X_ROT = 1u << 0,      // shift rotates through C (bit 0: C & flags & 1 is the rotate-in bit)
     X_SHL = 1u << 1,
@@ -86,8 +96,12 @@ enum : uint32_t {
 struct Entry2 {
     uint32_t w[16];
 };
+// Quad-major table: q[k][op] holds words 4k..4k+3 of opcode op's entry.
+struct alignas(16) EntryQuad {
+    uint32_t w[4];
+};
 struct EntryTable2 {
-    Entry2 e[256];
+    EntryQuad q[4][256];
 };
 
 namespace dt {
@@ -110,25 +124,25 @@ constexpr Entry2 expand2(uint64_t w) {
     f |= base == 2 ? X_IND : 0u;
     f |= bit ? X_BIT : 0u;
     const uint32_t len = illegal ? 1u : F(w, D_LEN, 2) + 1u;
-    e.w[0] = f | (len << 16) | (F(w, D_CYC, 3) << 24);
+    e.w[E_FLAGS] = f | (len << 16) | (F(w, D_CYC, 3) << 24);
     const uint32_t idx_byte = stack ? 3u : idx == 1 ? 1u : idx == 2 ? 2u : 4u;
     const uint32_t xind_byte = F(w, D_INDX, 1) ? 1u : 4u;
-    e.w[1] = (0x4440u | idx_byte) | ((0x4440u | xind_byte) << 16);
-    e.w[2] = stack || base == 2 ? 0u : base == 0 ? 0xFFu : 0xFFFFu;
-    e.w[3] = stack && F(w, D_PULL, 1) ? 1u : 0u;
-    e.w[4] = (stack || F(w, D_ZPW, 1)) ? 0xFFu : 0xFFFFu;
-    e.w[5] = stack ? 0x100u : 0u;
+    e.w[E_SELIDX] = (0x4440u | idx_byte) | ((0x4440u | xind_byte) << 16);
+    e.w[E_BASEM] = stack || base == 2 ? 0u : base == 0 ? 0xFFu : 0xFFFFu;
+    e.w[E_ADDK] = stack && F(w, D_PULL, 1) ? 1u : 0u;
+    e.w[E_WRAP] = (stack || F(w, D_ZPW, 1)) ? 0xFFu : 0xFFFFu;
+    e.w[E_ORV] = stack ? 0x100u : 0u;
     const uint32_t opa_byte = opa == A_A ? 0u : opa == A_X ? 1u : opa == A_Y ? 2u : opa == A_SP ? 3u
                               : opa == A_M ? 4u : opa == A_PHP ? 5u : 6u;
-    e.w[6] = 0x6660u | opa_byte;
+    e.w[E_SELA] = 0x6660u | opa_byte;
     const bool bm = F(w, D_BM, 1), bx = F(w, D_BX, 1);
-    e.w[7] = bm ? (bx ? 0xFFFFFFFFu : 1u) : 0u;
-    e.w[8] = (bx ? 0xFFu : 0u) + (F(w, D_CIN1, 1) ? 1u : 0u);
-    e.w[9] = F(w, D_CINC, 1) ? 1u : 0u;
-    e.w[10] = unit == U_ADD ? 0x1FFu : 0u;
+    e.w[E_BMUL] = bm ? (bx ? 0xFFFFFFFFu : 1u) : 0u;
+    e.w[E_BADD] = (bx ? 0xFFu : 0u) + (F(w, D_CIN1, 1) ? 1u : 0u);
+    e.w[E_CINM] = F(w, D_CINC, 1) ? 1u : 0u;
+    e.w[E_SUMM] = unit == U_ADD ? 0x1FFu : 0u;
     const bool logic_and = unit == U_AND || unit == U_OR, logic_xor = unit == U_XOR || unit == U_OR;
     const bool shifter = unit == U_SHL || unit == U_SHR;
-    e.w[11] = (logic_and ? 0xFFu : 0u) | ((logic_xor ? 0xFFu : 0u) << 8) | ((shifter ? 0x1FFu : 0u) << 16);
+    e.w[E_LOGIC] = (logic_and ? 0xFFu : 0u) | ((logic_xor ? 0xFFu : 0u) << 8) | ((shifter ? 0x1FFu : 0u) << 16);
     uint32_t comp = flg == F_NZ ? 0x82u : flg == F_NZC ? 0x83u : flg == F_NZCV ? 0xC3u : 0u;
     if (bit) comp = 0xC2u;
     uint32_t keep = 0xFFu & ~comp & ~fcm;
@@ -136,12 +150,12 @@ constexpr Entry2 expand2(uint64_t w) {
     uint32_t from_r = 0;
     if (flg || bit || fcm) set |= 0x20u;  // set_flag forces the unused bit (cpu.hpp:52-59)
     if (wp) { keep = 0; comp = 0; from_r = 0xEFu; set |= 0x20u; }  // PLP: (pulled | $20) & ~$10
-    e.w[12] = keep | (comp << 8) | (set << 16) | (from_r << 24);
+    e.w[E_PMASK] = keep | (comp << 8) | (set << 16) | (from_r << 24);
     const uint32_t brmask = br ? (1u << F(w, D_BRF, 3)) : 0u;
-    e.w[13] = br ? (F(w, D_BRP, 1) ? brmask : 0u) : 0x100u;
+    e.w[E_BRVAL] = br ? (F(w, D_BRP, 1) ? brmask : 0u) : 0x100u;
     const uint32_t spd = F(w, D_SPD, 2);
-    e.w[14] = (brmask | 0x100u) | ((spd == 1 ? 0xFFu : spd == 2 ? 0x01u : 0u) << 24);
-    e.w[15] = (F(w, D_WA, 1) ? 0xFFu : 0u) | (F(w, D_WX, 1) ? 0xFF00u : 0u) | (F(w, D_WY, 1) ? 0xFF0000u : 0u) |
+    e.w[E_BRMASK] = (brmask | 0x100u) | ((spd == 1 ? 0xFFu : spd == 2 ? 0x01u : 0u) << 24);
+    e.w[E_WMASK] = (F(w, D_WA, 1) ? 0xFFu : 0u) | (F(w, D_WX, 1) ? 0xFF00u : 0u) | (F(w, D_WY, 1) ? 0xFF0000u : 0u) |
               (F(w, D_WSP, 1) ? 0xFF000000u : 0u);
     return e;
 }
@@ -149,27 +163,34 @@ constexpr Entry2 expand2(uint64_t w) {
 constexpr EntryTable2 build_entries2() {
     EntryTable2 t{};
     const DecodeTable d = build();
-    for (int i = 0; i < 256; ++i) t.e[i] = expand2(d.e[i]);
+    for (int i = 0; i < 256; ++i) {
+        const Entry2 e = expand2(d.e[i]);
+        for (int k = 0; k < 4; ++k)
+            for (int j = 0; j < 4; ++j) t.q[k][i].w[j] = e.w[4 * k + j];
+    }
     return t;
 }
 }  // namespace dt
 
 constexpr EntryTable2 kEntries2Host = dt::build_entries2();
 
-NESLE_HD void load_entry2(const Entry2* table, uint32_t op, Entry2& e) {
-#if defined(__CUDA_ARCH__)
-    const uint4* src = reinterpret_cast<const uint4*>(&table[op]);
+// Quarters [q0, q1) of opcode op's entry into w[4 * q0 ...].
+template <uint32_t q0, uint32_t q1>
+NESLE_HD void load_quads(const EntryQuad* table, uint32_t op, uint32_t* w) {
+    if constexpr (q1 > q0) {
 #pragma unroll
-    for (uint32_t q = 0; q < 4; ++q) {
-        const uint4 v = src[q];
-        e.w[4 * q + 0] = v.x;
-        e.w[4 * q + 1] = v.y;
-        e.w[4 * q + 2] = v.z;
-        e.w[4 * q + 3] = v.w;
-    }
+        for (uint32_t q = q0; q < q1; ++q) {
+#if defined(__CUDA_ARCH__)
+            const uint4 v = reinterpret_cast<const uint4*>(table)[q * 256u + op];
+            w[4 * q + 0] = v.x;
+            w[4 * q + 1] = v.y;
+            w[4 * q + 2] = v.z;
+            w[4 * q + 3] = v.w;
 #else
-    e = table[op];
+            for (uint32_t j = 0; j < 4; ++j) w[4 * q + j] = table[q * 256u + op].w[j];
 #endif
+        }
+    }
 }
 
 // Bytes op | b1 << 8 | b2 << 16 (| junk << 24) at `pc` in the shared PRG copy;
@@ -185,40 +206,42 @@ NESLE_HD uint32_t fetch_bytes(const Ctx& c, uint32_t pc) {
 NESLE_HD uint32_t fetch_bytes_bus(const Ctx& c, Lane& L) {
     L.pc &= 0xFFFFu;
     const uint32_t op = io_rd(c, L, L.pc);
-    const uint32_t len = (c.dec2[op].w[0] >> 16) & 3u;
+    const uint32_t len = (c.dec2[op].w[E_FLAGS] >> 16) & 3u;  // quarter 0 holds E_FLAGS
     const uint32_t b1 = len >= 2 ? io_rd(c, L, (L.pc + 1) & 0xFFFF) : 0u;
     const uint32_t b2 = len >= 3 ? io_rd(c, L, (L.pc + 2) & 0xFFFF) : 0u;
     return op | (b1 << 8) | (b2 << 16);
 }
 
 // One instruction (bytes `nb`, entry `E`) on the uniform datapath; returns its
-// cycles.  On return `nb` holds the next instruction's bytes and `fresh`
-// says whether they are valid (prefetched from the PRG window, no NMI due).
+// cycles.  On return `nb` holds the next instruction's bytes, `early` the
+// first kEarlyQuads quarters of their entry, and `fresh` says whether they are
+// valid (prefetched from the PRG window, no NMI due).
 // The program counter may exceed $FFFF transiently (pc + length, branch
 // targets): such a value is never in the PRG window, so it always goes
 // through the loop top, which masks it.
-template <bool kSharedRam>
-NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, const Entry2& E, bool& fresh) {
-    const uint32_t pc = L.pc, R = L.R, P = L.p, f = E.w[0], bytes = nb;
+template <bool kSharedRam, uint32_t kEarlyQuads>
+NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, uint32_t* early, const Entry2& E, bool& fresh) {
+    const uint32_t pc = L.pc, R = L.R, P = L.p, f = E.w[E_FLAGS], bytes = nb;
     const uint32_t b16 = prmt(bytes, 0u, 0x4421u);
 
     // ---- next PC (flags from the previous instruction), prefetch ----
     const uint32_t seq = pc + ((f >> 16) & 3u);
     const uint32_t target = seq + prmt(bytes, 0u, 0x9991u);  // + sign-extended b1
-    const bool taken = ((P ^ E.w[13]) & E.w[14]) == 0u;  // P ^ w13 < $200: w14's SP byte drops out
+    const bool taken = ((P ^ E.w[E_BRVAL]) & E.w[E_BRMASK]) == 0u;  // P ^ E_BRVAL < $200: the SP byte drops out
     uint32_t npc = taken ? target : seq;
     npc = (f & X_JMP) ? b16 : npc;
     const uint32_t branch_cyc = taken ? 1u + (((seq ^ target) >> 8) & 1u) : 0u;
     nb = fetch_bytes(c, npc);
+    load_quads<0, kEarlyQuads>(c.dec2, nb & 0xFFu, early);
 
     // ---- effective address ----
-    const uint32_t idx = prmt(R, 0u, E.w[1]);
-    uint32_t base = b16 & E.w[2];
+    const uint32_t idx = prmt(R, 0u, E.w[E_SELIDX]);
+    uint32_t base = b16 & E.w[E_BASEM];
     if (f & X_IND) {
-        const uint32_t zp = (bytes >> 8) + prmt(R, 0u, E.w[1] >> 16);
+        const uint32_t zp = (bytes >> 8) + prmt(R, 0u, E.w[E_SELIDX] >> 16);
         base = ram_rd(c, zp & 0xFFu) | (ram_rd(c, (zp + 1u) & 0xFFu) << 8);
     }
-    const uint32_t addr = ((base + idx + E.w[3]) & E.w[4]) | E.w[5];
+    const uint32_t addr = ((base + idx + E.w[E_ADDK]) & E.w[E_WRAP]) | E.w[E_ORV];
     const uint32_t page = (((base ^ addr) & f) >> 8) & 1u;  // X_PAGE is bit 8
     const uint32_t cyc = (f >> 24) + branch_cyc + page;
 
@@ -244,24 +267,24 @@ NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, const Entry2& E, 
 
     // ---- ALU ----
     const uint32_t pool = (P | 0x30u) * 256u + m;                 // {m, P|$30, 0, 0}
-    const uint32_t opa = prmt(R, pool, E.w[6]);
-    const uint32_t opb = m * E.w[7] + E.w[8];
-    const uint32_t sum = opa + opb + (P & 1u) * E.w[9];
+    const uint32_t opa = prmt(R, pool, E.w[E_SELA]);
+    const uint32_t opb = m * E.w[E_BMUL] + E.w[E_BADD];
+    const uint32_t sum = opa + opb + (P & 1u) * E.w[E_CINM];
     const uint32_t rotc = f & P & 1u;                              // X_ROT is bit 0
     const uint32_t shl9 = opa * 2u + rotc;                         // result, out bit at 8
     const uint32_t t9 = rotc * 256u + opa;
     const uint32_t shr9 = (t9 * 513u) >> 1;                        // (t9 >> 1) | (t9 & 1) << 8
     const uint32_t sh9 = (f & X_SHL) ? shl9 : shr9;
-    const uint32_t w11 = E.w[11];
-    const uint32_t r9 = (sum & E.w[10]) | (opa & m & w11) | ((opa ^ m) & (w11 >> 8) & 0xFFu) | (sh9 & (w11 >> 16));
+    const uint32_t lg = E.w[E_LOGIC];
+    const uint32_t r9 = (sum & E.w[E_SUMM]) | (opa & m & lg) | ((opa ^ m) & (lg >> 8) & 0xFFu) | (sh9 & (lg >> 16));
     const uint32_t r = r9 & 0xFFu;
 
     // ---- flags: P = (P & keep) | (computed & comp) | set | (r & from_r) ----
     const uint32_t vbit = ((~(opa ^ opb) & (opa ^ r)) >> 1) & 0x40u;
     const uint32_t nv = (f & X_BIT) ? (m & 0xC0u) : ((r & 0x80u) | vbit);
     const uint32_t computed = nv | (r == 0u ? 0x02u : 0u) | (r9 >> 8);
-    const uint32_t w12 = E.w[12];
-    const uint32_t p = (P & w12) | (computed & (w12 >> 8) & 0xFFu) | ((w12 >> 16) & 0xFFu) | (r & (w12 >> 24));
+    const uint32_t pm = E.w[E_PMASK];
+    const uint32_t p = (P & pm) | (computed & (pm >> 8) & 0xFFu) | ((pm >> 16) & 0xFFu) | (r & (pm >> 24));
 
     // ---- memory write ----
     if (wm && is_ram) *ram_byte = (uint8_t)r;
@@ -272,7 +295,7 @@ NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, const Entry2& E, 
     if (wm && !(is_ram || (is_prg && !c.prg_writes) || is_ctrl)) io_wr(c, L, addr, r);
 
     // ---- register write-back ----
-    L.R = ((R & ~E.w[15]) | (prmt(r, 0u, 0u) & E.w[15])) + (E.w[14] & 0xFF000000u);
+    L.R = ((R & ~E.w[E_WMASK]) | (prmt(r, 0u, 0u) & E.w[E_WMASK])) + (E.w[E_BRMASK] & 0xFF000000u);
     L.p = p;
     L.pc = npc;
     fresh = in_prg_window(c, npc) && !L.nmi;
@@ -280,11 +303,17 @@ NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, const Entry2& E, 
 }
 
 // All frames of one env-step on the v2 datapath (run_frames' structure: the
-// loop top, NMI entry and bus fetches on the rare path).
-template <bool kSharedRam>
+// loop top, NMI entry and bus fetches on the rare path).  kEarlyQuads (0, 1
+// or 2) quarters of the next entry are prefetched one iteration ahead, the
+// rest loaded at the top of the iteration: prefetching hides a shared-memory
+// load behind the current instruction but keeps 4 registers per quarter live
+// across the loop, so the best depth depends on the kernel's other register
+// pressure and on how much memory latency it already waits for.
+template <bool kSharedRam, uint32_t kEarlyQuads>
 NESLE_HD void run_frames_v2(const Ctx& c, Lane& L) {
     uint32_t nb = 0;
     bool fresh = false;
+    Entry2 E;  // quarters below kEarlyQuads: prefetched with nb (valid with fresh); the rest per iteration
     for (;;) {
         uint32_t it_cyc = 0;
         if (!fresh || L.pending >= L.horizon || L.instr >= c.max_instr) {
@@ -298,14 +327,14 @@ NESLE_HD void run_frames_v2(const Ctx& c, Lane& L) {
             }
             if (!fresh) {
                 nb = in_prg_window(c, L.pc) ? fetch_bytes(c, L.pc) : fetch_bytes_bus(c, L);
+                load_quads<0, kEarlyQuads>(c.dec2, nb & 0xFFu, E.w);
                 fresh = true;
             }
         }
         const uint32_t pc = L.pc, op = nb & 0xFFu;
-        Entry2 E;
-        load_entry2(c.dec2, op, E);
-        if (E.w[0] & X_SIDE) {
-            if (E.w[0] & X_ILLEGAL) {
+        load_quads<kEarlyQuads, 4>(c.dec2, op, E.w);
+        if (E.w[E_FLAGS] & X_SIDE) {
+            if (E.w[E_FLAGS] & X_ILLEGAL) {
                 // The reference executes `trap` (cpu.hpp:716-720); the env stops instead.
                 L.status_word = NESLE_STATUS_ILLEGAL | (op << 16) | pc;
                 L.cycles += it_cyc;
@@ -313,11 +342,19 @@ NESLE_HD void run_frames_v2(const Ctx& c, Lane& L) {
                 continue;
             }
             exec_special(c, L, op, (nb >> 8) & 0xFFu, (nb >> 16) & 0xFFu);
-            it_cyc += (E.w[0] >> 24) & 0xFu;
+            it_cyc += (E.w[E_FLAGS] >> 24) & 0xFu;
             fresh = in_prg_window(c, L.pc) && !L.nmi;
-            if (fresh) nb = fetch_bytes(c, L.pc);
+            if (fresh) {
+                nb = fetch_bytes(c, L.pc);
+                load_quads<0, kEarlyQuads>(c.dec2, nb & 0xFFu, E.w);
+            }
         } else {
-            it_cyc += exec_v2<kSharedRam>(c, L, nb, E, fresh);
+            uint32_t next[8];
+            it_cyc += exec_v2<kSharedRam, kEarlyQuads>(c, L, nb, next, E, fresh);
+            if constexpr (kEarlyQuads > 0) {
+#pragma unroll
+                for (uint32_t j = 0; j < 4 * kEarlyQuads; ++j) E.w[j] = next[j];
+            }
         }
         it_cyc += L.dma;
         L.dma = 0;
@@ -331,12 +368,12 @@ NESLE_HD void run_frames_v2(const Ctx& c, Lane& L) {
     }
 }
 
-template <bool kSharedRam = true>
+template <bool kSharedRam, uint32_t kEarlyQuads>
 NESLE_HD void run_env_step_v2(const Ctx& c, EnvRecord& rec, uint8_t action, float& reward, uint8_t& done) {
     Lane L;
     load_lane(L, rec, action);
     begin_step(L);
-    run_frames_v2<kSharedRam>(c, L);
+    run_frames_v2<kSharedRam, kEarlyQuads>(c, L);
     reward_done(c, L, reward, done);
     store_lane(L, rec);
 }

@@ -60,6 +60,7 @@ class HostCore(_Common):
     _h_lib = None
     global_ram = False  # subclass HostCoreGlobal runs the in-place RAM variant
     v2 = True           # the v2 datapath (nes_v2.cuh); the V1 subclasses run the first one
+    early = 0           # v2: execution-entry quarters prefetched one iteration ahead (0-2)
 
     @classmethod
     def lib(cls):
@@ -76,6 +77,7 @@ class HostCore(_Common):
             lib.host_copy_field.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_uint64]
             lib.host_set_global_ram.argtypes = [ctypes.c_void_p, ctypes.c_int]
             lib.host_set_v2.argtypes = [ctypes.c_void_p, ctypes.c_int]
+            lib.host_set_early.argtypes = [ctypes.c_void_p, ctypes.c_int]
             cls._h_lib = lib
         return cls._h_lib
 
@@ -90,6 +92,7 @@ class HostCore(_Common):
         self._h = h
         self.lib().host_set_global_ram(h, int(self.global_ram))
         self.lib().host_set_v2(h, int(self.v2))
+        self.lib().host_set_early(h, int(self.early))
 
     def __del__(self):
         if getattr(self, "_h", None):
@@ -134,6 +137,15 @@ class HostCoreHybrid(HostCore):
 
 class HostCoreHybridStack(HostCore):
     global_ram = 3  # in place, stack page in a separate slot
+
+
+class HostCoreEarly1(HostCore):
+    early = 1  # shared RAM, one entry quarter prefetched
+
+
+class HostCoreInterleavedEarly2(HostCore):
+    global_ram = 2
+    early = 2  # the interleaved placement's datapath: zero page in a slot, two quarters prefetched
 
 
 class HostCoreV1(HostCore):

@@ -37,6 +37,7 @@ struct HostBatch {
     bool hybrid = false;      // ... with one page in a separate slot (hybrid placement)
     bool async = false;       // ... with operands loaded ahead (run_frames_async, HostAsync)
     bool v2 = true;           // the v2 datapath (nes_v2.cuh), as the product's unprofiled kernels
+    uint32_t early = 0;       // v2: entry quarters prefetched one iteration ahead (0-2)
     uint32_t slot_page = 0;   // the slot's page: 0x000 or 0x100
     std::vector<uint8_t> smem_ram = std::vector<uint8_t>(kSlots * kRamBytes);
 };
@@ -52,6 +53,13 @@ void unstage(HostBatch& h, uint32_t env, uint32_t slot) {
         h.ram[(size_t)env * kRamBytes + a] = h.smem_ram[(a & 0x7FC) * kSlots + slot * 4 + (a & 3)];
 }
 }  // namespace
+
+template <bool kSharedRam>
+static void step_v2(uint32_t early, const Ctx& c, EnvRecord& rec, uint8_t action, float& reward, uint8_t& done) {
+    if (early == 2) run_env_step_v2<kSharedRam, 2>(c, rec, action, reward, done);
+    else if (early == 1) run_env_step_v2<kSharedRam, 1>(c, rec, action, reward, done);
+    else run_env_step_v2<kSharedRam, 0>(c, rec, action, reward, done);
+}
 
 extern "C" {
 
@@ -135,6 +143,7 @@ void host_set_global_ram(void* p, int on) {
 }
 
 void host_set_v2(void* p, int on) { static_cast<HostBatch*>(p)->v2 = on != 0; }
+void host_set_early(void* p, int quads) { static_cast<HostBatch*>(p)->early = (uint32_t)quads; }
 
 void host_reset(void* p) {
     auto* h = static_cast<HostBatch*>(p);
@@ -175,7 +184,7 @@ void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) 
         c.slots = h->global_ram ? 1 : kSlots;
         c.prg = h->prg.data();
         c.dec = dec;
-        c.dec2 = dec_table2.e;
+        c.dec2 = &dec_table2.q[0][0];
         c.view = &h->v;
         c.env = e;
         c.frameskip = h->v.frameskip;
@@ -206,13 +215,13 @@ void host_step(void* p, const uint8_t* actions, int device_api, int auto_reset) 
                 A.state ^= e * 0x85EBCA6Bu;  // a different idle pattern per env
                 run_env_step_async(c, rec, actions[e], reward, done, A);
             } else if (h->v2) {
-                run_env_step_v2<false>(c, rec, actions[e], reward, done);
+                step_v2<false>(h->early, c, rec, actions[e], reward, done);
             } else {
                 run_env_step<false>(c, rec, actions[e], reward, done);
             }
             if (h->hybrid) memcpy(h->ram.data() + (size_t)e * kRamBytes + c.zpage, zp, 256);
         } else {
-            if (h->v2) run_env_step_v2<true>(c, rec, actions[e], reward, done);
+            if (h->v2) step_v2<true>(h->early, c, rec, actions[e], reward, done);
             else run_env_step<true>(c, rec, actions[e], reward, done);
             unstage(*h, e, slot);
         }

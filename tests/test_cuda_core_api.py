@@ -100,7 +100,7 @@ def test_properties(torch):
     assert hasattr(b, "step_device") and hasattr(b, "ram_device")  # native_ppo's bridge check
     assert b.step_kernel_placement == "shared"  # small batches stage RAM in shared memory
     big = CudaBatch(40000, 4, wl1.rom.image, device=0)
-    assert big.step_kernel_placement == "hybrid"
+    assert big.step_kernel_placement == "interleaved"  # large batches: every env resident, RAM interleaved
 
 
 @pytest.mark.gpu

@@ -371,3 +371,9 @@ def test_unsupported_boards_are_rejected():
     bad = kat.board_image(1, bytes(32768), bytes(8192))  # MMC1
     with pytest.raises(ValueError, match="supported cartridges"):
         GpuCore(4, 1, bad)
+
+
+def test_unknown_placement_is_rejected(monkeypatch):
+    monkeypatch.setenv("NESLE_STEP_KERNEL", "registers")
+    with pytest.raises(ValueError, match="unknown placement 'registers'"):
+        GpuCore(4, 1, kat.board_image(0, bytes(32768), bytes(8192)))
