@@ -862,6 +862,13 @@ cudaError_t configure_kernels() {
     if (e == cudaSuccess) e = configure_global<kStepGlobalPreload>();
     if (e == cudaSuccess) e = configure_global<kStepHybridPreload>();
     if (e == cudaSuccess) e = configure_global<kStepInterleavedPreload>();
+    // step_profile's instantiations (above the 48 KB default with the 16 KB v2 table reserved)
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(step_kernel_global<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(kPrgSmem + kDecSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(step_kernel_global<true, false, 0, false, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kPrgSmem + kDecSmem));
     return e;
 }
 
