@@ -1,8 +1,10 @@
 // kernels.cu -- sm_100a kernels of the batched NES core.
 //
-//   step_kernel_global  one env-step per thread, env RAM in place; with kHybrid
-//                   the zero page is staged in shared memory (the default
-//                   above two shared-memory waves, e.g. at 65,536 envs)
+//   step_kernel_global  one env-step per thread, every env resident; with kHybrid
+//                   the zero page is staged in shared memory, with kInterleave
+//                   the rest of RAM lives for the launch in an env-interleaved
+//                   working copy (kHybrid + kInterleave: the default above two
+//                   shared-memory waves, e.g. at 65,536 envs)
 //   step_kernel     one env-step per thread, env RAM staged in shared memory
 //                   (the default for small batches, e.g. 2,048 envs)
 //   reset_kernel    masked or full snapshot/cold reset
@@ -320,7 +322,8 @@ step_kernel_global(const BatchView* __restrict__ vp, const uint8_t* __restrict__
             DevicePreload A;
             run_env_step_async(c, rec, action, reward, done, A);
         } else if (kV2) {
-            run_env_step_v2<false, kInterleave ? kEarlyInterleaved : kEarlyInPlace>(c, rec, action, reward, done);
+            run_env_step_v2<false, kInterleave ? kEarlyInterleaved : kEarlyInPlace, kInterleave>(c, rec, action, reward,
+                                                                                                 done);
         } else {
             run_env_step<false>(c, rec, action, reward, done);
         }

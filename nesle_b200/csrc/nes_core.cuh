@@ -4,7 +4,9 @@
 // 6502: every opcode executes the same instruction stream (fetch, table
 // decode, effective address, one memory read, a combined adder/logic/shifter,
 // one memory write, register/flag write-back), with the differences between
-// opcodes carried as data in a 64-bit decode word.  Lanes of a warp that sit at
+// opcodes carried as data in a decode table (this file's 32-byte entries for
+// the first datapath and the profiled kernel; nes_v2.cuh's 64-byte entries for
+// the production kernels).  Lanes of a warp that sit at
 // different PCs therefore stay converged through the common path; only I/O
 // accesses, NMI entry, PPU event settlement, OAM DMA and the stack-transfer
 // instructions (JSR/RTS/RTI/BRK/JMP-indirect) take divergent side paths.
@@ -18,11 +20,13 @@
 // whole row is staged in shared memory in a bank-interleaved layout -- byte
 // `a` of the env in slot `s` of a CTA with `S` slots is at
 // ((a & 0x7FC) * S + s * 4 + (a & 3)), so slot s always hits bank s % 32 and
-// no RAM access of a warp bank-conflicts (small batches) -- or the row stays
-// in place in global memory, optionally with one page (the zero page by
-// default) staged in an interleaved shared-memory slot (large batches, the
-// default at 65,536 envs).  PRG ROM (32 KB) and the execution entries are
-// staged once per CTA into shared memory in every placement.
+// no RAM access of a warp bank-conflicts (small batches) -- or one page (the
+// zero page by default) is staged in an interleaved shared-memory slot and the
+// rest is used in place: in the env's row, or (the default for large batches,
+// e.g. 65,536 envs) in a working copy in global memory interleaved the same
+// way, so a warp's accesses to one address are one 128-byte line.  PRG ROM
+// (32 KB) and the execution entries are staged once per CTA into shared
+// memory in every placement.
 //
 // The header also compiles as plain C++ (NESLE_HD expands to nothing) so the
 // same code can be unit-tested on the CPU against the checker.

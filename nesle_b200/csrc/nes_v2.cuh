@@ -219,7 +219,7 @@ NESLE_HD uint32_t fetch_bytes_bus(const Ctx& c, Lane& L) {
 // The program counter may exceed $FFFF transiently (pc + length, branch
 // targets): such a value is never in the PRG window, so it always goes
 // through the loop top, which masks it.
-template <bool kSharedRam, uint32_t kEarlyQuads>
+template <bool kSharedRam, uint32_t kEarlyQuads, bool kSameStride = false>
 NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, uint32_t* early, const Entry2& E, bool& fresh) {
     const uint32_t pc = L.pc, R = L.R, P = L.p, f = E.w[E_FLAGS], bytes = nb;
     const uint32_t b16 = prmt(bytes, 0u, 0x4421u);
@@ -238,8 +238,15 @@ NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, uint32_t* early, 
     const uint32_t idx = prmt(R, 0u, E.w[E_SELIDX]);
     uint32_t base = b16 & E.w[E_BASEM];
     if (f & X_IND) {
-        const uint32_t zp = (bytes >> 8) + prmt(R, 0u, E.w[E_SELIDX] >> 16);
-        base = ram_rd(c, zp & 0xFFu) | (ram_rd(c, (zp + 1u) & 0xFFu) << 8);
+        // The two pointer bytes at zp and zp + 1 (wrapping in the zero page) as
+        // two word loads and a funnel shift, from wherever page 0 lives: the
+        // slot, or c.ram (interleaved shared row, or the row in place, stride 1).
+        const uint32_t zp = ((bytes >> 8) + prmt(R, 0u, E.w[E_SELIDX] >> 16)) & 0xFFu;
+        const bool zs = c.zp && c.zpage == 0u;
+        const uint32_t* zw = reinterpret_cast<const uint32_t*>(zs ? c.zp : c.ram);
+        const uint32_t st = zs ? c.zslots : c.slots;
+        const uint32_t w0 = zw[(zp >> 2) * st], w1 = zw[(((zp >> 2) + 1u) & 63u) * st];
+        base = NESLE_FUNNEL(w0, w1, zp * 8u) & 0xFFFFu;
     }
     const uint32_t addr = ((base + idx + E.w[E_ADDK]) & E.w[E_WRAP]) | E.w[E_ORV];
     const uint32_t page = (((base ^ addr) & f) >> 8) & 1u;  // X_PAGE is bit 8
@@ -248,7 +255,10 @@ NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, uint32_t* early, 
     // ---- operand ----
     const bool rd = (f & X_RD) != 0, wm = (f & X_WM) != 0;
     const bool is_ram = addr < 0x2000u, is_prg = addr >= c.prg_lo, is_ctrl = addr == 0x4016u;
-    uint8_t* ram_byte = ram_ptr(c, addr);
+    // kSameStride (interleaved placement): the zero-page slot and the working
+    // copy share the lane stride, so one offset serves both and only the base
+    // is selected.
+    uint8_t* ram_byte = kSameStride ? ((addr & 0x700u) == 0u ? c.zp : c.ram) + ram_off(c, addr) : ram_ptr(c, addr);
     uint32_t mem;
     if (kSharedRam) {
         const uint8_t* src = is_ram ? ram_byte : c.prg + (addr & 0x7FFF);
@@ -309,7 +319,7 @@ NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, uint32_t* early, 
 // load behind the current instruction but keeps 4 registers per quarter live
 // across the loop, so the best depth depends on the kernel's other register
 // pressure and on how much memory latency it already waits for.
-template <bool kSharedRam, uint32_t kEarlyQuads>
+template <bool kSharedRam, uint32_t kEarlyQuads, bool kSameStride = false>
 NESLE_HD void run_frames_v2(const Ctx& c, Lane& L) {
     uint32_t nb = 0;
     bool fresh = false;
@@ -350,7 +360,7 @@ NESLE_HD void run_frames_v2(const Ctx& c, Lane& L) {
             }
         } else {
             uint32_t next[8];
-            it_cyc += exec_v2<kSharedRam, kEarlyQuads>(c, L, nb, next, E, fresh);
+            it_cyc += exec_v2<kSharedRam, kEarlyQuads, kSameStride>(c, L, nb, next, E, fresh);
             if constexpr (kEarlyQuads > 0) {
 #pragma unroll
                 for (uint32_t j = 0; j < 4 * kEarlyQuads; ++j) E.w[j] = next[j];
@@ -368,12 +378,12 @@ NESLE_HD void run_frames_v2(const Ctx& c, Lane& L) {
     }
 }
 
-template <bool kSharedRam, uint32_t kEarlyQuads>
+template <bool kSharedRam, uint32_t kEarlyQuads, bool kSameStride = false>
 NESLE_HD void run_env_step_v2(const Ctx& c, EnvRecord& rec, uint8_t action, float& reward, uint8_t& done) {
     Lane L;
     load_lane(L, rec, action);
     begin_step(L);
-    run_frames_v2<kSharedRam, kEarlyQuads>(c, L);
+    run_frames_v2<kSharedRam, kEarlyQuads, kSameStride>(c, L);
     reward_done(c, L, reward, done);
     store_lane(L, rec);
 }

@@ -159,9 +159,12 @@ class PPOTrainer:
 
             for p in self.model.parameters():
                 dist.broadcast(p.data, src=0)
-        # CUDA-graph the minibatch update on one GPU (capturable Adam keeps its
-        # step counters on the device)
-        self.use_graphs = world == 1 and use_graphs
+        # CUDA-graph the minibatch update (capturable Adam keeps its step
+        # counters on the device).  Across GPUs it is two graphs around one
+        # NCCL all-reduce of a flat gradient buffer, so no collective is
+        # captured.
+        self.use_graphs = use_graphs
+        self._split_graphs = world > 1
         self._graph = None
         self._eager_steps = 0
         self.opt = torch.optim.Adam(self.model.parameters(), lr=config.learning_rate, eps=1e-5,
@@ -229,15 +232,22 @@ class PPOTrainer:
         return loss.detach()
 
     def _graph_step(self, b, idx):
-        """One minibatch update as a CUDA graph replay (single GPU): the minibatch
-        is gathered into static buffers, then forward, backward, clipping and the
-        Adam step replay from one captured graph."""
+        """One minibatch update as CUDA graph replays: the minibatch is gathered
+        into static buffers, then forward, backward, clipping and the Adam step
+        replay from one captured graph.  With split graphs the gradients land in
+        one flat buffer, which is all-reduced between the backward graph and the
+        clip + Adam graph."""
         import torch
+        import torch.distributed as dist
 
         g = self._graph
         for name, src in zip(("obs", "act", "logp", "adv", "ret"), b):
             torch.index_select(src, 0, idx, out=g[name])
         g["graph"].replay()
+        if "step_graph" in g:
+            if self.world > 1:
+                dist.all_reduce(g["flat"])
+            g["step_graph"].replay()
         return g["loss"].detach().clone()
 
     def _capture(self, b, idx):
@@ -247,20 +257,42 @@ class PPOTrainer:
         static = {name: torch.index_select(src, 0, idx)
                   for name, src in zip(("obs", "act", "logp", "adv", "ret"), b)}
         graph = torch.cuda.CUDAGraph()
-        self.opt.zero_grad(set_to_none=True)
-        with torch.cuda.graph(graph):
-            loss = self._minibatch_loss(static["obs"], static["act"], static["logp"], static["adv"], static["ret"])
-            loss.backward()
-            torch.nn.utils.clip_grad_norm_(params, self.cfg.max_grad_norm)
-            self.opt.step()
+        if self._split_graphs:
+            # every gradient a view of one flat buffer (backward accumulates into
+            # it in place), so the all-reduce is one call on contiguous memory
+            flat = torch.zeros(sum(p.numel() for p in params), dtype=params[0].dtype, device=self.dev)
+            off = 0
+            for p in params:
+                p.grad = flat[off:off + p.numel()].view_as(p)
+                off += p.numel()
+            with torch.cuda.graph(graph):
+                flat.zero_()
+                loss = self._minibatch_loss(static["obs"], static["act"], static["logp"], static["adv"],
+                                            static["ret"])
+                loss.backward()
+            step_graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(step_graph):
+                flat.mul_(1.0 / self.world)
+                torch.nn.utils.clip_grad_norm_(params, self.cfg.max_grad_norm)
+                self.opt.step()
+            static["flat"] = flat
+            static["step_graph"] = step_graph
+        else:
+            self.opt.zero_grad(set_to_none=True)
+            with torch.cuda.graph(graph):
+                loss = self._minibatch_loss(static["obs"], static["act"], static["logp"], static["adv"],
+                                            static["ret"])
+                loss.backward()
+                torch.nn.utils.clip_grad_norm_(params, self.cfg.max_grad_norm)
+                self.opt.step()
         static["loss"] = loss
         static["graph"] = graph
         self._graph = static
 
     def update(self) -> dict[str, Any]:
         """GAE + update_epochs passes of clipped-surrogate minibatch updates.
-        On one GPU the minibatch step replays a captured CUDA graph after a few
-        eager warm-up steps; across GPUs it stays eager (NCCL all-reduce)."""
+        The minibatch step replays captured CUDA graphs after a few eager
+        warm-up steps (across GPUs, two graphs around the NCCL all-reduce)."""
         import torch
 
         cfg = self.cfg

@@ -118,8 +118,11 @@ def test_training_runs_and_env_side_replays_on_checker():
 
 
 @pytest.mark.gpu
-def test_graphed_update_matches_eager_update():
-    """The single-GPU CUDA-graph update replays the eager minibatch step."""
+@pytest.mark.parametrize("split", [False, True])
+def test_graphed_update_matches_eager_update(split):
+    """The CUDA-graph update replays the eager minibatch step: one graph (one
+    GPU), or the two graphs that run around the gradient all-reduce across GPUs
+    (split, here with a world of one)."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     from nesle_b200 import build
@@ -130,6 +133,7 @@ def test_graphed_update_matches_eager_update():
     out = []
     for graphs in (False, True):
         tr = PPOTrainer(cfg, use_graphs=graphs)  # reseeds: identical init and rollout
+        tr._split_graphs = split
         tr.rollout()
         stats = tr.update()
         out.append((tr.obs_buf.cpu(), float(stats["loss"]), [p.detach().cpu() for p in tr.model.parameters()],
