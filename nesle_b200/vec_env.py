@@ -189,10 +189,10 @@ class NesleVecEnv:
             obs = self._obs_cache if self._obs_cache is not None else self._frames()
             copied = False
         dones, trunc = self._done_and_truncation(dones)
-        infos = [self._info(observation_cadence=self.observation_cadence, observations_copied=copied,
-                            observations_stale=not copied,
-                            rgb_observations_copied=copied and self.observation_mode == "rgb_array")
-                 for _ in range(self.num_envs)]
+        base = self._info(observation_cadence=self.observation_cadence, observations_copied=copied,
+                          observations_stale=not copied,
+                          rgb_observations_copied=copied and self.observation_mode == "rgb_array")
+        infos = [base.copy() for _ in range(self.num_envs)]  # one dict per env (SB3 adds keys per env)
         if dones.any():
             idx = np.nonzero(dones)[0]
             for i in idx:
@@ -217,7 +217,8 @@ class NesleVecEnv:
         self._launch(masks)
         _, rewards, dones = self._step_outputs(with_ram=False)
         dones, trunc = self._done_and_truncation(dones)
-        infos = [self._info(observations_copied=False) for _ in range(self.num_envs)]
+        base = self._info(observations_copied=False)
+        infos = [base.copy() for _ in range(self.num_envs)]
         if dones.any():
             idx = np.nonzero(dones)[0]
             terminal = self._rows(idx)
