@@ -43,12 +43,14 @@ constexpr uint32_t kDecSmem = NESLE_V2 ? sizeof(EntryTable2) : 256 * sizeof(Entr
 // Execution-entry quarters the v2 datapath prefetches one iteration ahead, per
 // placement.  B200, env-steps/s with 0 / 1 / 2 quarters: shared RAM, 2,048
 // envs of config 2: 240 / 247 / 244 k; hybrid, 65,536 envs of config 4:
-// 2.27 / 2.27 / 2.18 M (2 spills), config 2: 3.26 / 3.15 / 3.13 M;
-// interleaved, config 4: 2.31 / 2.34 / 2.36 M, config 2: 3.37 / 3.35 / 3.29 M.
-// Config 4 is the benchmark workload.
+// 2.27 / 2.27 / 2.18 M (2 spills), config 2: 3.26 / 3.15 / 3.13 M.  For the
+// interleaved kernel the best depth moved with the datapath: 2 quarters won
+// config 4 before the word-load pointer read (2.36 M against 2.34 / 2.31 M
+// with 1 / 0), 1 quarter wins after it (2.50 M against 2.47 M; config 2 3.42
+// against 3.31 M).  Config 4 is the benchmark workload.
 constexpr uint32_t kEarlyShared = 1;
 constexpr uint32_t kEarlyInPlace = 0;
-constexpr uint32_t kEarlyInterleaved = 2;
+constexpr uint32_t kEarlyInterleaved = 1;
 
 // Stages the execution entries of the datapath the kernel runs (v2 when
 // kV2) into shared memory at `dst`.

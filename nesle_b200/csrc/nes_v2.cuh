@@ -18,7 +18,7 @@
 //    9-bit value with the shifted-out bit at bit 8, like the adder's carry, so
 //    one carry extraction serves both units;
 //  * the next instruction's three bytes are prefetched one iteration ahead,
-//    and with them, per kernel, the first one or two 16-byte quarters of its
+//    and with them, per kernel, none, one or two 16-byte quarters of its
 //    entry (the fields the next-PC and address stages read first); the rest
 //    (ALU, flags, write-back) is loaded at the top of its own iteration, where
 //    the address stage hides its latency;

@@ -143,9 +143,14 @@ class HostCoreEarly1(HostCore):
     early = 1  # shared RAM, one entry quarter prefetched
 
 
-class HostCoreInterleavedEarly2(HostCore):
+class HostCoreHybridEarly1(HostCore):
     global_ram = 2
-    early = 2  # the interleaved placement's datapath: zero page in a slot, two quarters prefetched
+    early = 1  # the interleaved placement's datapath: zero page in a slot, one quarter prefetched
+
+
+class HostCoreHybridEarly2(HostCore):
+    global_ram = 2
+    early = 2  # the deepest prefetch the datapath supports
 
 
 class HostCoreV1(HostCore):

@@ -7,14 +7,14 @@ import pytest
 
 import kat_roms as kat
 from harness import (STATE_FIELDS, HostCore, HostCoreEarly1, HostCoreGlobal, HostCoreGlobalAsync, HostCoreHybrid,
-                     HostCoreHybridAsync, HostCoreHybridStack, HostCoreHybridV1, HostCoreInterleavedEarly2,
-                     HostCoreV1, assert_same, run_lockstep)
+                     HostCoreHybridAsync, HostCoreHybridEarly1, HostCoreHybridEarly2, HostCoreHybridStack,
+                     HostCoreHybridV1, HostCoreV1, assert_same, run_lockstep)
 from nesle_b200 import workloads as w
 from oracle import Oracle
 
 # Every RAM placement of the step kernel, each compiled for the CPU.
 ALL_CORES = [HostCore, HostCoreGlobal, HostCoreHybrid, HostCoreHybridStack, HostCoreGlobalAsync, HostCoreHybridAsync,
-             HostCoreEarly1, HostCoreInterleavedEarly2, HostCoreV1, HostCoreHybridV1]
+             HostCoreEarly1, HostCoreHybridEarly1, HostCoreHybridEarly2, HostCoreV1, HostCoreHybridV1]
 
 
 @pytest.mark.parametrize("make,auto_reset", [(w.config1, False), (w.config2, True), (w.config3, True),
