@@ -302,13 +302,19 @@ NESLE_HD uint32_t exec_v2(const Ctx& c, Lane& L, uint32_t& nb, uint32_t* early, 
     const bool latch = cw && ((r | L.cstrobe) & 1u);
     L.csr = latch ? L.action : L.csr;
     L.cstrobe = cw ? (r & 1u) : L.cstrobe;
-    if (wm && !(is_ram || (is_prg && !c.prg_writes) || is_ctrl)) io_wr(c, L, addr, r);
+    // The NMI line is clear on entry (the loop top consumes it), and an I/O
+    // write ($2000) is the only way this path can raise it.
+    bool nmi_clear = true;
+    if (wm && !(is_ram || (is_prg && !c.prg_writes) || is_ctrl)) {
+        io_wr(c, L, addr, r);
+        nmi_clear = !L.nmi;
+    }
 
     // ---- register write-back ----
     L.R = ((R & ~E.w[E_WMASK]) | (prmt(r, 0u, 0u) & E.w[E_WMASK])) + (E.w[E_BRMASK] & 0xFF000000u);
     L.p = p;
     L.pc = npc;
-    fresh = in_prg_window(c, npc) && !L.nmi;
+    fresh = in_prg_window(c, npc) && nmi_clear;
     return cyc;
 }
 
