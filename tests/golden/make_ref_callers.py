@@ -29,6 +29,7 @@ Usage (needs the reference tree and a built ``oracle/_ref``)::
 from __future__ import annotations
 
 import hashlib
+import os
 import sys
 import tempfile
 import types
@@ -37,7 +38,8 @@ from pathlib import Path
 import numpy as np
 
 ROOT = Path(__file__).resolve().parents[2]
-REF_SRC = Path("/root/reference/src")
+# The reference checkout: NESLE_REFERENCE, else a sibling of this repository (as oracle/Makefile).
+REF_SRC = Path(os.environ.get("NESLE_REFERENCE", ROOT.parent / "reference")) / "src"
 OUT = Path(__file__).with_name("ref_callers.npz")
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(ROOT / "tests"))
