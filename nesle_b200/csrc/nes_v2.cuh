@@ -2,10 +2,10 @@
 //
 // Same semantics as exec_uniform / run_frames in nes_core.cuh (cpu.hpp:378-730,
 // kernels.cu:19-104), fewer integer-pipe instructions per emulated
-// instruction.  The step kernel is integer-pipe bound at the occupancy a
-// 65,536-env batch allows (ncu: the ALU pipe busy two thirds of the time, 169
-// ALU-pipe warp instructions per warp iteration); this version spends them on
-// the computation instead of on unpacking table fields:
+// instruction.  The first datapath kept the ALU pipe busy two thirds of the
+// time at the occupancy a 65,536-env batch allows (ncu: 169 ALU-pipe warp
+// instructions per warp iteration), much of it unpacking table fields; this
+// one spends the pipe on the computation:
 //
 //  * a 64-byte execution entry per opcode (Entry2) holds every field as an
 //    operand the datapath uses directly: byte-permute selectors (PRMT) that
@@ -24,7 +24,9 @@
 //    the address stage hides its latency;
 //  * the table is stored quad-major (four 16-byte quarters, each an array over
 //    the 256 opcodes), so lanes of one warp loading different opcodes spread
-//    over all 32 banks instead of colliding on a 64-byte stride.
+//    over all 32 banks instead of colliding on a 64-byte stride;
+//  * the (zp,X) / (zp),Y pointer is two word loads and a funnel shift, so the
+//    indirect modes add a handful of instructions, not two routed byte reads.
 //
 // The header compiles as plain C++ too (the host unit-test build), like
 // nes_core.cuh.
