@@ -7,6 +7,8 @@ full 65,536-env configuration.
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -377,3 +379,14 @@ def test_unknown_placement_is_rejected(monkeypatch):
     monkeypatch.setenv("NESLE_STEP_KERNEL", "registers")
     with pytest.raises(ValueError, match="unknown placement 'registers'"):
         GpuCore(4, 1, kat.board_image(0, bytes(32768), bytes(8192)))
+
+
+@pytest.mark.parametrize("variant", ["interleaved", "global-async", "hybrid-preload"])
+def test_boards_fall_back_to_the_hybrid_placement(variant, monkeypatch):
+    """Placements without a board instantiation run UxROM / CNROM batches on
+    the hybrid kernel (shared and global are kept as asked)."""
+    monkeypatch.setenv("NESLE_STEP_KERNEL", variant)
+    g = GpuCore(8, 2, kat.UXROM_ROM)
+    info = _lib.Info()
+    _lib.check(g.lib.nesle_get_info(g._h, ctypes.byref(info)))
+    assert _lib.PLACEMENTS[info.step_placement] == "hybrid"
