@@ -178,21 +178,23 @@ class NesleVecEnv:
         self._step_count += 1
         self._steps += 1
         self._launch(masks)
-        ram, rewards, dones = self._step_outputs(with_ram=self.observation_mode == "ram")
-        copied = True
-        if self.observation_mode == "ram":
+        ram_mode = self.observation_mode == "ram"
+        copied = ram_mode or self.observation_cadence <= 1 or self._step_count % self.observation_cadence == 0
+        # The info dicts do not depend on the step's results, so they are built
+        # while the step runs on the GPU: one dict per env (SB3 adds keys per env).
+        base = self._info(observation_cadence=self.observation_cadence, observations_copied=copied,
+                          observations_stale=not copied,
+                          rgb_observations_copied=copied and self.observation_mode == "rgb_array")
+        infos = [base.copy() for _ in range(self.num_envs)]
+        ram, rewards, dones = self._step_outputs(with_ram=ram_mode)
+        if ram_mode:
             obs = ram
-        elif self.observation_cadence <= 1 or self._step_count % self.observation_cadence == 0:
+        elif copied:
             obs = self._frames()
             self._obs_cache = obs
         else:
             obs = self._obs_cache if self._obs_cache is not None else self._frames()
-            copied = False
         dones, trunc = self._done_and_truncation(dones)
-        base = self._info(observation_cadence=self.observation_cadence, observations_copied=copied,
-                          observations_stale=not copied,
-                          rgb_observations_copied=copied and self.observation_mode == "rgb_array")
-        infos = [base.copy() for _ in range(self.num_envs)]  # one dict per env (SB3 adds keys per env)
         if dones.any():
             idx = np.nonzero(dones)[0]
             for i in idx:
@@ -215,10 +217,10 @@ class NesleVecEnv:
         masks = self._masks(actions)
         self._steps += 1
         self._launch(masks)
+        base = self._info(observations_copied=False)
+        infos = [base.copy() for _ in range(self.num_envs)]  # built while the step runs
         _, rewards, dones = self._step_outputs(with_ram=False)
         dones, trunc = self._done_and_truncation(dones)
-        base = self._info(observations_copied=False)
-        infos = [base.copy() for _ in range(self.num_envs)]
         if dones.any():
             idx = np.nonzero(dones)[0]
             terminal = self._rows(idx)
