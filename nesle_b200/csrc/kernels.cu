@@ -493,6 +493,13 @@ __device__ __forceinline__ RenderEnv stage_snapshot(const BatchView& v, uint32_t
 // 40 and 48): both are issue-bound with a barrier per phase, so occupancy
 // pays; 6 and 5 measured best (gray84 is limited to 5 by shared memory).
 constexpr int kRenderMinBlocks = 6, kGrayMinBlocks = 5;
+// Bit k of x (k < 8) moved to bit 4k: the 8 bits spread over the nibbles.
+__device__ __forceinline__ uint32_t spread_nibbles(uint32_t x) {
+    x = (x | (x << 12)) & 0x000F000Fu;
+    x = (x | (x << 6)) & 0x03030303u;
+    return (x | (x << 3)) & 0x11111111u;
+}
+
 // Sprite-free pixels of one 8-column segment: row y, columns 8 c8 .. 8 c8 + 7,
 // packed one per byte (pixel p in byte p % 4 of out[p / 4]).  `tiles` are the
 // row's tile entries (slot j = scrolled tile column (sx >> 3) + j); a pixel is
@@ -513,13 +520,13 @@ __device__ __forceinline__ uint64_t segment_background(const RenderEnv& e, const
         grp1 = (e1 >> 16) & 3u;
         keep = 8u - fine;
     }
+    // All 8 pixels with two byte permutes: selector nibble p is pixel p's
+    // pattern value (0-3), plus 4 (a byte of w1) from pixel `keep` on.
+    const uint32_t sel = spread_nibbles(__brev(lo8) >> 24) | (spread_nibbles(__brev(hi8) >> 24) << 1) |
+                         (uint32_t)(0x44444444ull << (4u * keep));
     const uint32_t w0 = group[grp0], w1 = group[grp1];
-    out[0] = out[1] = 0u;
-#pragma unroll
-    for (uint32_t p = 0; p < 8; ++p) {
-        const uint32_t col = ((lo8 >> (7 - p)) & 1u) | (((hi8 >> (7 - p)) & 1u) << 1);
-        out[p >> 2] |= __byte_perm(p < keep ? w0 : w1, 0u, 0x4440u | col) << (8 * (p & 3));
-    }
+    out[0] = __byte_perm(w0, w1, sel & 0xFFFFu);
+    out[1] = __byte_perm(w0, w1, sel >> 16);
     return ((s.mask & 0x10) && ((s.mask & 0x04) || c8 != 0)) ? (sm.rows[y] & sm.cols[c8]) : 0ull;
 }
 
