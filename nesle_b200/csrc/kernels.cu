@@ -493,6 +493,14 @@ __device__ __forceinline__ RenderEnv stage_snapshot(const BatchView& v, uint32_t
 // 40 and 48): both are issue-bound with a barrier per phase, so occupancy
 // pays; 6 and 5 measured best (gray84 is limited to 5 by shared memory).
 constexpr int kRenderMinBlocks = 6, kGrayMinBlocks = 5;
+// Bits 0-3 of x as the bytes of a word: bit k -> byte k = 0xFF.
+__device__ __forceinline__ uint32_t byte_mask(uint32_t x) {
+    return (((x & 0xFu) * 0x00204081u) & 0x01010101u) * 0xFFu;
+}
+
+// The 4 bytes of a byte-compare result (0xFF or 0 each) as bits 0-3.
+__device__ __forceinline__ uint32_t byte_flags(uint32_t m) { return ((m & 0x08040201u) * 0x01010101u) >> 24; }
+
 // Bit k of x (k < 8) moved to bit 4k: the 8 bits spread over the nibbles.
 __device__ __forceinline__ uint32_t spread_nibbles(uint32_t x) {
     x = (x | (x << 12)) & 0x000F000Fu;
@@ -563,17 +571,18 @@ __device__ __forceinline__ uint64_t sprite_segment(const RenderEnv& e, const Sna
         grp1 = (e1 >> 16) & 3u;
         keep = 8u - fine;
     }
-    uint64_t bg = 0;    // background colour index of pixel p in byte p (0: transparent)
-    uint32_t bgop = 0;  // bit p: the background a behind-background sprite is tested against is non-zero
-#pragma unroll
-    for (uint32_t p = 0; p < 8; ++p) {
-        const uint32_t col = ((lo8 >> (7 - p)) & 1u) | (((hi8 >> (7 - p)) & 1u) << 1);
-        const uint32_t bgc = col ? sm.res[(p < keep ? grp0 : grp1) * 4u + col] : 0u;
-        bg |= (uint64_t)bgc << (8 * p);
-        bgop |= (bgc != 0u ? 1u : 0u) << p;
-    }
+    // Background colour indices of the 8 pixels, pixel p in byte p (0:
+    // transparent): two byte permutes over the groups' raw palette words
+    // (byte 0 zero, bytes 1-3 the group's colours), as in segment_background.
+    const uint32_t* res32 = reinterpret_cast<const uint32_t*>(sm.res);
+    const uint32_t sel = spread_nibbles(__brev(lo8) >> 24) | (spread_nibbles(__brev(hi8) >> 24) << 1) |
+                         (uint32_t)(0x44444444ull << (4u * keep));
+    const uint32_t r0 = res32[grp0] & 0xFFFFFF00u, r1 = res32[grp1] & 0xFFFFFF00u;
+    const uint32_t bg_lo = __byte_perm(r0, r1, sel & 0xFFFFu), bg_hi = __byte_perm(r0, r1, sel >> 16);
+    // bit p: the background a behind-background sprite is tested against is non-zero
+    uint32_t bgop = byte_flags(__vcmpne4(bg_lo, 0u)) | (byte_flags(__vcmpne4(bg_hi, 0u)) << 4);
     bool bgop_ready = (int)y >= e.split;  // above the split the reference tests the lower view's background
-    uint64_t spc = 0;                      // colour of the claiming sprite, byte p
+    uint32_t spc_lo = 0, spc_hi = 0;       // colour of the claiming sprite, byte p
     uint32_t claimed = 0;
     while (spr && claimed != 0xFFu) {
         const uint32_t i = lowest_set(spr);
@@ -601,18 +610,25 @@ __device__ __forceinline__ uint64_t sprite_segment(const RenderEnv& e, const Sna
         }
         if (!take) continue;
         claimed |= take;
-        const uint8_t* pal = sm.res + 0x10 + (attr & 3u) * 4u;
-#pragma unroll
-        for (uint32_t p = 0; p < 8; ++p)
-            if ((take >> p) & 1u) spc |= (uint64_t)pal[((plo >> p) & 1u) | (((phi >> p) & 1u) << 1)] << (8 * p);
+        // The sprite palette's colours of its 8 pixels (pixel p's pattern
+        // value in selector nibble p), kept where the sprite takes the pixel.
+        const uint32_t pw = res32[4u + (attr & 3u)];
+        const uint32_t ssel = spread_nibbles(plo) | (spread_nibbles(phi) << 1);
+        spc_lo |= __byte_perm(pw, 0u, ssel & 0xFFFFu) & byte_mask(take & 0xFu);
+        spc_hi |= __byte_perm(pw, 0u, ssel >> 16) & byte_mask(take >> 4);
     }
+    // Claimed pixels show the sprite; the others the background, or the
+    // backdrop res[0] where the background is transparent.
+    const uint32_t back = (uint32_t)sm.res[0] * 0x01010101u;
+    const uint32_t c_lo = (spc_lo & byte_mask(claimed & 0xFu)) |
+                          ((bg_lo | (back & ~__vcmpne4(bg_lo, 0u))) & ~byte_mask(claimed & 0xFu));
+    const uint32_t c_hi = (spc_hi & byte_mask(claimed >> 4)) |
+                          ((bg_hi | (back & ~__vcmpne4(bg_hi, 0u))) & ~byte_mask(claimed >> 4));
+    if (!kLuma) return (uint64_t)c_lo | ((uint64_t)c_hi << 32);
     uint64_t out = 0;
 #pragma unroll
-    for (uint32_t p = 0; p < 8; ++p) {
-        const uint32_t b = (uint32_t)(bg >> (8 * p)) & 0xFFu;
-        const uint32_t c = ((claimed >> p) & 1u) ? (uint32_t)(spc >> (8 * p)) & 0xFFu : (b ? b : (uint32_t)sm.res[0]);
-        out |= (uint64_t)(kLuma ? (uint32_t)lut[c] : c) << (8 * p);
-    }
+    for (uint32_t p = 0; p < 8; ++p)
+        out |= (uint64_t)lut[((p < 4 ? c_lo : c_hi) >> (8 * (p & 3))) & 0xFFu] << (8 * p);
     return out;
 }
 
