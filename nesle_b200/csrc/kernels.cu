@@ -463,6 +463,7 @@ struct SnapSmem {
     uint64_t cols[kFrameW / 8];
     uint16_t spat[64 * 16];  // sprite pattern rows, flips applied
 };
+static_assert(offsetof(SnapSmem, res) % 4 == 0, "the resolved palette is read as 4-byte words");
 
 __device__ __forceinline__ RenderEnv stage_snapshot(const BatchView& v, uint32_t env, SnapSmem& sm) {
     const uint32_t tid = threadIdx.x;
@@ -493,6 +494,7 @@ __device__ __forceinline__ RenderEnv stage_snapshot(const BatchView& v, uint32_t
 // 40 and 48): both are issue-bound with a barrier per phase, so occupancy
 // pays; 6 and 5 measured best (gray84 is limited to 5 by shared memory).
 constexpr int kRenderMinBlocks = 6, kGrayMinBlocks = 5;
+
 // Bits 0-3 of x as the bytes of a word: bit k -> byte k = 0xFF.
 __device__ __forceinline__ uint32_t byte_mask(uint32_t x) {
     return (((x & 0xFu) * 0x00204081u) & 0x01010101u) * 0xFFu;
