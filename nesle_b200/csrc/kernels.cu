@@ -463,7 +463,8 @@ struct SnapSmem {
     uint64_t cols[kFrameW / 8];
     uint16_t spat[64 * 16];  // sprite pattern rows, flips applied
 };
-static_assert(offsetof(SnapSmem, res) % 4 == 0, "the resolved palette is read as 4-byte words");
+static_assert(offsetof(SnapSmem, res) % 4 == 0 && offsetof(SnapSmem, oam) % 4 == 0,
+              "the resolved palette and the OAM entries are read as 4-byte words");
 
 __device__ __forceinline__ RenderEnv stage_snapshot(const BatchView& v, uint32_t env, SnapSmem& sm) {
     const uint32_t tid = threadIdx.x;
@@ -589,9 +590,9 @@ __device__ __forceinline__ uint64_t sprite_segment(const RenderEnv& e, const Sna
     while (spr && claimed != 0xFFu) {
         const uint32_t i = lowest_set(spr);
         spr &= spr - 1;
-        const uint8_t* so = s.oam + i * 4;
-        const int d = (int)so[3] - (int)x0;  // segment pixel of the sprite's column 0 (-7..7)
-        const uint32_t pat = sm.spat[i * 16 + (y - so[0] - 1)];
+        const uint32_t so = reinterpret_cast<const uint32_t*>(sm.oam)[i];  // Y, tile, attributes, X
+        const int d = (int)(so >> 24) - (int)x0;  // segment pixel of the sprite's column 0 (-7..7)
+        const uint32_t pat = sm.spat[i * 16 + (y - (so & 0xFFu) - 1)];
         uint32_t plo = pat & 0xFFu, phi = pat >> 8;  // sprite pixel sx at bit sx
         if (d >= 0) {
             plo = (plo << d) & 0xFFu;
@@ -601,7 +602,7 @@ __device__ __forceinline__ uint64_t sprite_segment(const RenderEnv& e, const Sna
             phi >>= -d;
         }
         uint32_t take = (plo | phi) & ~claimed;
-        const uint32_t attr = so[2];
+        const uint32_t attr = (so >> 16) & 0xFFu;
         if (take && (attr & 0x20)) {
             if (!bgop_ready) {
                 bgop = 0;
